@@ -1,0 +1,120 @@
+/* C ABI of libpowersparse_b200.so: PowerSparse SpMM / SDDMM for B200 (sm_100a).
+ *
+ * This is the drop-in boundary.  Every entry point takes plain pointers and
+ * sizes; device pointers are CUDA device addresses on the device that was
+ * current when the matrix was created, and `stream` is a cudaStream_t (NULL =
+ * the legacy default stream).  The C++ operator API of the reference
+ * (include/PowerSparse_SpMM/PowerSparse_SpMM.h, include/PowerSparse_SDDMM/
+ * PowerSparse_SDDMM.h, include/utils/matrix_utils.h in this tree) is a thin
+ * layer over these functions.
+ *
+ * Each replaced reference interface is cited as path:line inside the
+ * ParCIS/PowerSparse source tree.
+ *
+ * Errors: every int-returning call returns PS_OK (0) or an error code and
+ * records a message readable with ps_last_error() (thread-local).
+ * PS_ERR_INVALID_ARGUMENT corresponds to the reference throwing
+ * std::invalid_argument, PS_ERR_CUDA to std::runtime_error from CUDA_CALL
+ * (utils/cuda_utils.h:7-14).
+ */
+#ifndef POWERSPARSE_B200_H
+#define POWERSPARSE_B200_H
+
+#include <stdbool.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct ps_matrix ps_matrix;
+
+enum {
+  PS_OK = 0,
+  PS_ERR_INVALID_ARGUMENT = 1,
+  PS_ERR_CUDA = 2,
+  PS_ERR_INTERNAL = 3
+};
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* ps_last_error(void);
+
+/* Library version string. */
+const char* ps_version(void);
+
+/* Preprocess a host CSR matrix into the block/residue worksets on the current
+ * device.  Replaces the constructor PowerSparseMatrixGPU(int row_num, int col_num,
+ * int nnz_num, const int* row_ptr, const int* col_ind, const float* sp_data)
+ * (utils/matrix_utils.h:22-23, utils/matrix_utils.cu:470-663): same validation,
+ * same error texts, bit-identical layout.  Synchronous. */
+int ps_matrix_create(int row_num, int col_num, int nnz_num, const int* row_ptr,
+                     const int* col_ind, const float* sp_data, ps_matrix** out);
+
+/* As ps_matrix_create, with the SM count of the workset heuristic
+ * (utils/matrix_utils.cu:37-42) given explicitly (sm_count <= 0: the device's).
+ * The layout then equals the reference's on a GPU with that many SMs. */
+int ps_matrix_create_sm(int row_num, int col_num, int nnz_num, const int* row_ptr,
+                        const int* col_ind, const float* sp_data, int sm_count,
+                        ps_matrix** out);
+
+/* Frees the worksets (~PowerSparseMatrixGPU, utils/matrix_utils.h:24, 43-55).
+ * Complete outstanding operator calls first.  NULL is ignored. */
+void ps_matrix_destroy(ps_matrix* matrix);
+
+/* Accessors of utils/matrix_utils.h:30-40 (same meaning, same pointer kinds:
+ * ps_matrix_group_num is a host array; the workset arrays are host arrays of
+ * device pointers; residue offset / atomic flags are device arrays). */
+int ps_matrix_row(const ps_matrix* matrix);             /* MatrixRow()        */
+int ps_matrix_col(const ps_matrix* matrix);             /* MatrixCol()        */
+int ps_matrix_nnz(const ps_matrix* matrix);             /* MatrixNNZ()        */
+int ps_matrix_group_type_num(const ps_matrix* matrix);  /* GroupTypeNum()     */
+int ps_matrix_group_fine_size(const ps_matrix* matrix); /* GroupFineSize()    */
+const int* ps_matrix_group_num(const ps_matrix* matrix);                   /* GroupNum()         */
+const int* const* ps_matrix_workset_col_ind(const ps_matrix* matrix);      /* WorksetColInd()    */
+const float* const* ps_matrix_workset_sp_data(const ps_matrix* matrix);    /* WorksetSpData()    */
+const int* const* ps_matrix_group_destination(const ps_matrix* matrix);    /* GroupDestination() */
+const int* ps_matrix_residue_offset(const ps_matrix* matrix);              /* ResidueOffset()    */
+const bool* ps_matrix_residue_atomic(const ps_matrix* matrix);             /* ResidueAtomic()    */
+
+/* Elements in workset s (residue: ResidueOffset()[GroupNum()[0]]; block s:
+ * GroupNum()[s] * GROUP_SIZE(s)), as benchmarks/benchmark.cu:147-154 sizes the
+ * SDDMM outputs.  Returns -1 for an invalid s. */
+long long ps_matrix_workset_size(const ps_matrix* matrix, int s);
+
+/* Wall time of the preprocessing in ps_matrix_create, milliseconds. */
+double ps_matrix_preprocess_ms(const ps_matrix* matrix);
+
+/* CUDA device the matrix lives on. */
+int ps_matrix_device(const ps_matrix* matrix);
+
+/* FP32 C (+)= A * B on `stream`, asynchronous.  B is [MatrixCol() x N] and C is
+ * [MatrixRow() x N], both row-major device arrays; zero C before each
+ * independent call.  N: positive multiple of 32 with N/32 <= 65535.  Replaces
+ * the kernel launches of PowerSparse::SpMM (PowerSparse_SpMM/PowerSparse_SpMM.h:14-17,
+ * PowerSparse_SpMM/spmm_solution.cu:7-34) with one fused launch.  Dense offsets
+ * are 64-bit, so the reference's rows*N, cols*N <= INT_MAX limit
+ * (utils/matrix_utils.h:72-76) does not apply. */
+int ps_spmm(const ps_matrix* matrix, int N, const float* B, float* C, void* stream);
+
+/* FP32 SDDMM on `stream`, asynchronous: for every element e of workset s,
+ * out[s][e] (+)= A_e * <lhs[row(e), :], rhs[col(e), :]>, outputs in workset order.
+ * lhs is [MatrixRow() x N], rhs [MatrixCol() x N], row-major device arrays; `out`
+ * is a HOST array of GroupTypeNum() device pointers, each sized
+ * ps_matrix_workset_size(s) (may be NULL for an empty workset); zero them before
+ * each independent call.  N is 32 or 128.  Replaces the kernel launches of
+ * PowerSparse::SDDMM (PowerSparse_SDDMM/PowerSparse_SDDMM.h:14-18,
+ * PowerSparse_SDDMM/sddmm_solution.cu:7-50) with one fused launch. */
+int ps_sddmm(const ps_matrix* matrix, int N, const float* lhs, const float* rhs,
+             float* const* out, void* stream);
+
+/* nnz-balanced contiguous row panels for `parts` GPUs: writes cuts[0..parts]
+ * with cuts[0] = 0, cuts[parts] = row_num, nondecreasing, panel p = rows
+ * [cuts[p], cuts[p+1]).  Cut p is the first row whose row_ptr reaches
+ * p * nnz / parts.  Host only.  No reference counterpart (the reference is
+ * single-GPU; its only device choice is benchmarks/benchmark.cu:116). */
+int ps_partition_rows(int row_num, const int* row_ptr, int parts, int* cuts);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* POWERSPARSE_B200_H */

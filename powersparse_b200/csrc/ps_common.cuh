@@ -1,0 +1,70 @@
+// Shared internals of libpowersparse_b200: status handling and small device helpers.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <stdexcept>
+#include <string>
+
+namespace psb {
+
+// Errors travel as C++ exceptions inside the library and become status codes
+// at the extern "C" boundary (ps_capi.cu).  The two kinds mirror the reference's
+// convention: std::invalid_argument for caller errors, std::runtime_error for
+// CUDA failures (utils/cuda_utils.h:7-14 of the reference).
+struct CudaError : std::runtime_error {
+  cudaError_t code;
+  CudaError(cudaError_t c, const std::string& what) : std::runtime_error(what), code(c) {}
+};
+
+inline void check_cuda(cudaError_t status, const char* expr, const char* file, int line) {
+  if (status != cudaSuccess)
+    throw CudaError(status, std::string(file) + ":" + std::to_string(line) + ": " + expr + ": " +
+                                cudaGetErrorString(status));
+}
+
+#define PSB_CUDA(call) ::psb::check_cuda((call), #call, __FILE__, __LINE__)
+#define PSB_LAUNCH_CHECK() ::psb::check_cuda(cudaGetLastError(), "kernel launch", __FILE__, __LINE__)
+
+constexpr int kWarp = 32;
+
+__host__ __device__ inline int ceil_div(int a, int b) { return (a + b - 1) / b; }
+__host__ __device__ inline long long ceil_div_ll(long long a, long long b) { return (a + b - 1) / b; }
+
+inline int bits_for(unsigned long long max_value) {
+  int b = 0;
+  while (b < 64 && (max_value >> b) != 0) ++b;
+  return b;
+}
+
+// A device buffer owned by the library (freed on scope exit, also on throw).
+template <typename T>
+struct DeviceArray {
+  T* ptr = nullptr;
+  size_t count = 0;
+  DeviceArray() = default;
+  explicit DeviceArray(size_t n) { reset(n); }
+  DeviceArray(const DeviceArray&) = delete;
+  DeviceArray& operator=(const DeviceArray&) = delete;
+  DeviceArray(DeviceArray&& o) noexcept : ptr(o.ptr), count(o.count) { o.ptr = nullptr; o.count = 0; }
+  DeviceArray& operator=(DeviceArray&& o) noexcept {
+    if (this != &o) { release(); ptr = o.ptr; count = o.count; o.ptr = nullptr; o.count = 0; }
+    return *this;
+  }
+  ~DeviceArray() { release(); }
+  void reset(size_t n) {
+    release();
+    count = n;
+    if (n) PSB_CUDA(cudaMalloc(reinterpret_cast<void**>(&ptr), n * sizeof(T)));
+  }
+  void release() noexcept {
+    if (ptr) cudaFree(ptr);
+    ptr = nullptr;
+    count = 0;
+  }
+  T* release_ownership() { T* p = ptr; ptr = nullptr; count = 0; return p; }
+  T* get() const { return ptr; }
+};
+
+}  // namespace psb

@@ -1,0 +1,548 @@
+// GPU preprocessing: host CSR -> PowerSparse block/residue worksets (sm_100a).
+//
+// Produces, bit for bit, the layout of the reference constructor
+// PowerSparseMatrixGPU::PowerSparseMatrixGPU (utils/matrix_utils.cu:470-663):
+//
+//   step                               reference                  here
+//   S from the SM count                AnalyzeMatrix :31-63        workset_size_counts (1 pass)
+//   column histogram                   host OpenMP :508-514        col_histogram
+//   (row asc, col_nnz desc) stable     thrust::sort NNZPoint :522  64-bit key LSD radix sort
+//   groups per workset / metadata      host loops :132-208         row_group_counts + scans + scatter
+//   column -> signature bit            GenerateSigBit :65-128      same host std::sort call
+//   group signatures                   Get*Signature :261-327      group_signatures (all worksets)
+//   signature order (stable, per word) thrust::stable_sort :590    32-bit key LSD radix per word
+//   per-group column order (stable)    thrust::sort NNZPoint2 :616 (group, col) key LSD radix sort
+//   permuted offsets / final arrays    :451-464, :619-656          permute + gather kernels
+//
+// Every reference sort is stable with an integer key, so each becomes a radix
+// sort over exactly the bits in use; the resulting orders are identical.
+#include "ps_common.cuh"
+#include "ps_matrix.h"
+#include "ps_sort.cuh"
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <limits>
+#include <memory>
+#include <numeric>
+#include <stdexcept>
+
+namespace psb {
+
+Matrix::~Matrix() {
+  for (auto p : col_ind) cudaFree(p);
+  for (auto p : sp_data) cudaFree(p);
+  for (auto p : group_des) cudaFree(p);
+  cudaFree(residue_offset);
+  cudaFree(residue_atomic);
+  cudaFree(tasks);
+}
+
+namespace {
+
+constexpr int kSizeClasses = 26;  // group sizes 32 << k, k < 26, cover every 32-bit row length
+
+struct WorksetArrays {
+  int* des[kMaxWorksets];
+  int* start[kMaxWorksets];
+  uint32_t* sig[kMaxWorksets];
+  int groups[kMaxWorksets];
+};
+
+__device__ __forceinline__ int dev_group_size(int s) { return 32 << (s - 1); }
+
+// Sum over rows of floor(len / (32 << k)) for every k (AnalyzeMatrix's counts).
+__global__ void workset_size_counts(const int* __restrict__ row_ptr, int rows,
+                                    unsigned long long* __restrict__ counts) {
+  unsigned long long local[kSizeClasses];
+#pragma unroll
+  for (int k = 0; k < kSizeClasses; ++k) local[k] = 0;
+  for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < rows; r += gridDim.x * blockDim.x) {
+    const unsigned len = unsigned(row_ptr[r + 1] - row_ptr[r]);
+#pragma unroll
+    for (int k = 0; k < kSizeClasses; ++k) local[k] += len >> (5 + k);
+  }
+#pragma unroll
+  for (int k = 0; k < kSizeClasses; ++k) {
+    unsigned long long v = local[k];
+    for (int d = 16; d > 0; d >>= 1) v += __shfl_down_sync(0xffffffffu, v, d);
+    if ((threadIdx.x & 31) == 0 && v) atomicAdd(&counts[k], v);
+  }
+}
+
+__global__ void col_histogram(const int* __restrict__ col_ind, long long nnz, int* __restrict__ col_nnz) {
+  for (long long p = blockIdx.x * (long long)blockDim.x + threadIdx.x; p < nnz;
+       p += (long long)gridDim.x * blockDim.x)
+    atomicAdd(&col_nnz[col_ind[p]], 1);
+}
+
+// Sort-A keys: (row << wc) | (maxcnt - col_nnz[col]); ascending = row asc, frequency desc.
+__global__ void freq_sort_keys(const int* __restrict__ row_ptr, int rows, const int* __restrict__ col_ind,
+                               const int* __restrict__ col_nnz, int maxcnt, int wc,
+                               uint64_t* __restrict__ keys, uint32_t* __restrict__ vals) {
+  const int lane = threadIdx.x & 31;
+  const int warps = (gridDim.x * blockDim.x) >> 5;
+  for (int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < rows; r += warps) {
+    const int end = row_ptr[r + 1];
+    for (int p = row_ptr[r] + lane; p < end; p += 32) {
+      keys[p] = (uint64_t(r) << wc) | uint64_t(maxcnt - col_nnz[col_ind[p]]);
+      vals[p] = uint32_t(p);
+    }
+  }
+}
+
+// Groups of each row per workset (GetGroupNumArray, utils/matrix_utils.cu:132-156).
+__global__ void row_group_counts(const int* __restrict__ row_ptr, int rows, int S, int fine,
+                                 int* __restrict__ counts /* [S][rows] */) {
+  for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < rows; r += gridDim.x * blockDim.x) {
+    const int len = row_ptr[r + 1] - row_ptr[r];
+    if (S == 1) {
+      counts[r] = (len + fine - 1) / fine;
+      continue;
+    }
+    int rest = len;
+    for (int s = S - 1; s > 0; --s) {
+      const int g = rest / dev_group_size(s);
+      counts[size_t(s) * rows + r] = g;
+      rest -= g * dev_group_size(s);
+    }
+    counts[r] = rest > 0 ? 1 : 0;
+  }
+}
+
+// Source metadata of every group, in the reference's unpermuted group order
+// (GetGroupMetaInfo, utils/matrix_utils.cu:158-208): destination row, first
+// element in frequency-sorted order, and for the residue its size and atomic flag.
+__global__ void group_metadata(const int* __restrict__ row_ptr, int rows, int S, int fine,
+                               const int* __restrict__ prefix /* [S][rows+1] */, WorksetArrays wa,
+                               int* __restrict__ res_size, unsigned char* __restrict__ res_atomic) {
+  for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < rows; r += gridDim.x * blockDim.x) {
+    const int beg = row_ptr[r];
+    const int len = row_ptr[r + 1] - beg;
+    if (S == 1) {
+      const int groups = (len + fine - 1) / fine;
+      const int g0 = prefix[r];
+      for (int k = 0; k < groups; ++k) {
+        wa.des[0][g0 + k] = r;
+        wa.start[0][g0 + k] = beg + k * fine;
+        res_size[g0 + k] = min(len - k * fine, fine);
+        res_atomic[g0 + k] = groups > 1;
+      }
+      continue;
+    }
+    int at = beg, rest = len;
+    for (int s = S - 1; s > 0; --s) {
+      const int G = dev_group_size(s);
+      const int c = rest / G;
+      const int g0 = prefix[size_t(s) * (rows + 1) + r];
+      for (int k = 0; k < c; ++k) {
+        wa.des[s][g0 + k] = r;
+        wa.start[s][g0 + k] = at;
+        at += G;
+      }
+      rest -= c * G;
+    }
+    if (rest) {
+      const int g = prefix[r];
+      wa.des[0][g] = r;
+      wa.start[0][g] = at;
+      res_size[g] = rest;
+      res_atomic[g] = len > 32;
+    }
+  }
+}
+
+// Signature bits of every group of every workset (GetResidueSignature /
+// GetBlockSignature, utils/matrix_utils.cu:261-327).  One warp per row; element k
+// of the row (frequency order) belongs to the workset whose span contains it.
+__global__ void group_signatures(const int* __restrict__ row_ptr, int rows, int S, int fine,
+                                 const int* __restrict__ prefix, const uint32_t* __restrict__ perm,
+                                 const int* __restrict__ col_ind, const int* __restrict__ sigbit,
+                                 WorksetArrays wa) {
+  const int lane = threadIdx.x & 31;
+  const int warps = (gridDim.x * blockDim.x) >> 5;
+  for (int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < rows; r += warps) {
+    const int beg = row_ptr[r];
+    const int len = row_ptr[r + 1] - beg;
+    for (int k = lane; k < len; k += 32) {
+      int s = 0, g;
+      if (S == 1) {
+        g = prefix[r] + k / fine;
+      } else {
+        int rest = len, off = k;
+        g = -1;
+        for (int t = S - 1; t > 0; --t) {
+          const int G = dev_group_size(t);
+          const int c = rest / G;
+          if (off < c * G) {
+            s = t;
+            g = prefix[size_t(t) * (rows + 1) + r] + off / G;
+            break;
+          }
+          off -= c * G;
+          rest -= c * G;
+        }
+        if (g < 0) g = prefix[r];
+      }
+      const int b = sigbit[col_ind[perm[beg + k]]];
+      atomicOr(&wa.sig[s][size_t(b >> 5) * wa.groups[s] + g], 1u << (31 - (b & 31)));
+    }
+  }
+}
+
+__global__ void signature_word_keys(const uint32_t* __restrict__ sig_word, const uint32_t* __restrict__ idx,
+                                    int n, uint32_t* __restrict__ keys) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+    keys[i] = ~sig_word[idx[i]];  // ascending complement = descending word
+}
+
+__global__ void permute_residue_meta(const uint32_t* __restrict__ order, int G, const int* __restrict__ size,
+                                     const unsigned char* __restrict__ atomic_src, const int* __restrict__ des_src,
+                                     int* __restrict__ size_perm, bool* __restrict__ atomic_out,
+                                     int* __restrict__ des_out) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < G; i += gridDim.x * blockDim.x) {
+    const uint32_t j = order[i];
+    size_perm[i] = size[j];
+    atomic_out[i] = atomic_src[j] != 0;
+    des_out[i] = des_src[j];
+  }
+}
+
+__global__ void permute_block_des(const uint32_t* __restrict__ order, int G, const int* __restrict__ des_src,
+                                  int* __restrict__ des_out) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < G; i += gridDim.x * blockDim.x)
+    des_out[i] = des_src[order[i]];
+}
+
+// Element keys of one workset in final group order: (dst group << wcol) | col,
+// value = CSR position, written in frequency order within each group so that a
+// stable sort leaves equal columns in that order (thrust::sort of NNZPoint2).
+__global__ void gather_group_elements(const uint32_t* __restrict__ order, int G, int group_len,
+                                      const int* __restrict__ res_off, const int* __restrict__ res_size,
+                                      const int* __restrict__ start, const uint32_t* __restrict__ perm,
+                                      const int* __restrict__ col_ind, int wcol,
+                                      uint64_t* __restrict__ keys, uint32_t* __restrict__ vals) {
+  const int lane = threadIdx.x & 31;
+  const int warps = (gridDim.x * blockDim.x) >> 5;
+  for (int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; i < G; i += warps) {
+    const uint32_t j = order[i];
+    const long long dst = res_off ? (long long)res_off[i] : (long long)i * group_len;
+    const int size = res_off ? res_size[j] : group_len;
+    const int src = start[j];
+    for (int k = lane; k < size; k += 32) {
+      const uint32_t p = perm[src + k];
+      keys[dst + k] = (uint64_t(i) << wcol) | uint64_t(uint32_t(col_ind[p]));
+      vals[dst + k] = p;
+    }
+  }
+}
+
+__global__ void finalize_workset(const uint64_t* __restrict__ keys, const uint32_t* __restrict__ vals,
+                                 long long n, uint64_t col_mask, const float* __restrict__ sp_data,
+                                 int* __restrict__ col_out, float* __restrict__ val_out) {
+  for (long long q = blockIdx.x * (long long)blockDim.x + threadIdx.x; q < n;
+       q += (long long)gridDim.x * blockDim.x) {
+    col_out[q] = int(keys[q] & col_mask);
+    val_out[q] = sp_data[vals[q]];
+  }
+}
+
+unsigned grid_for(long long work, int per_block, int max_blocks) {
+  long long b = (work + per_block - 1) / per_block;
+  if (b < 1) b = 1;
+  if (b > max_blocks) b = max_blocks;
+  return unsigned(b);
+}
+
+// GenerateSigBit in FFC mode, ffc = 2 (utils/matrix_utils.cu:65-128, mode fixed at :55-60).
+// The column order comes from the same libstdc++ std::sort call on the same
+// input, so columns with equal frequency receive the same bits.
+void signature_bits(int cols, const std::vector<int>& col_nnz, std::vector<int>& bit, int& len) {
+  std::vector<int> by_freq(cols);
+  std::iota(by_freq.begin(), by_freq.end(), 0);
+  std::sort(by_freq.begin(), by_freq.end(),
+            [&col_nnz](const int& a, const int& b) { return col_nnz[a] > col_nnz[b]; });
+  bit.assign(cols, 0);
+  const int top = std::min(2, cols);
+  int next = 0;
+  long long budget = 0;
+  for (; next < top; ++next) {
+    bit[by_freq[next]] = 0;
+    budget += col_nnz[by_freq[next]];
+  }
+  int pos = 1;
+  while (next < cols) {
+    const int first = next;
+    long long run = 0;
+    while (next < cols) {
+      run += col_nnz[by_freq[next]];
+      if (run < budget || next == first) {
+        bit[by_freq[next]] = pos;
+        ++next;
+      } else {
+        break;
+      }
+    }
+    ++pos;
+  }
+  len = pos;
+  if (len < 32) len = 32;
+  else if (len % 32 < 16) len = (len / 32) * 32;
+  else len = (len / 32 + (len % 32 != 0)) * 32;
+  for (int c = 0; c < cols; ++c) bit[c] = std::min(bit[c], len - 1);
+}
+
+void validate_csr(int rows, int cols, int nnz, const int* row_ptr, const int* col_ind, const float* vals) {
+  // Same checks and messages as utils/matrix_utils.cu:475-488.
+  if (rows <= 0 || cols <= 0 || nnz <= 0 || rows > std::numeric_limits<int>::max() - 32 ||
+      nnz > std::numeric_limits<int>::max() - 32 || !row_ptr || !col_ind || !vals)
+    throw std::invalid_argument("Expected a nonempty CSR matrix with 32-bit indices");
+  if (row_ptr[0] != 0 || row_ptr[rows] != nnz) throw std::invalid_argument("Invalid CSR row-pointer endpoints");
+  for (int r = 0; r < rows; ++r)
+    if (row_ptr[r] < 0 || row_ptr[r] > row_ptr[r + 1])
+      throw std::invalid_argument("CSR row pointers must be nondecreasing");
+  for (int p = 0; p < nnz; ++p)
+    if (col_ind[p] < 0 || col_ind[p] >= cols || !std::isfinite(vals[p]))
+      throw std::invalid_argument("Invalid CSR column index or sparse value");
+}
+
+// Splits every workset into tasks of about kTaskElems elements, largest group
+// sizes first (the reference launches worksets S-1 down to 0).
+std::vector<Task> build_tasks(const Matrix& m, const std::vector<int>& h_res_off) {
+  std::vector<Task> tasks;
+  for (int s = m.S - 1; s >= 1; --s) {
+    const int G = group_size(s);
+    const int groups = m.group_num[s];
+    if (G >= kTaskElems) {
+      for (int g = 0; g < groups; ++g)
+        for (int off = 0; off < G; off += kTaskElems)
+          tasks.push_back({s, g * G + off, g * G + std::min(G, off + kTaskElems), g});
+    } else {
+      const int per = kTaskElems / G;
+      for (int g = 0; g < groups; g += per) {
+        const int ge = std::min(groups, g + per);
+        tasks.push_back({s, g * G, ge * G, g});
+      }
+    }
+  }
+  const int G0 = m.group_num[0];
+  int g = 0;
+  while (g < G0) {
+    const int first = g;
+    const int begin = h_res_off[g];
+    while (g < G0 && h_res_off[g + 1] - begin <= kTaskElems) ++g;
+    if (g == first) ++g;  // a single group longer than a task (cannot happen: <= 31 or 16)
+    tasks.push_back({0, begin, h_res_off[g], first});
+  }
+  return tasks;
+}
+
+}  // namespace
+
+Matrix* build_matrix(int rows, int cols, int nnz, const int* row_ptr, const int* col_ind,
+                     const float* sp_data, int sm_count) {
+  validate_csr(rows, cols, nnz, row_ptr, col_ind, sp_data);
+  const auto t0 = std::chrono::steady_clock::now();
+  std::unique_ptr<Matrix> m(new Matrix());
+  m->rows = rows;
+  m->cols = cols;
+  m->nnz = nnz;
+  PSB_CUDA(cudaGetDevice(&m->device));
+  if (sm_count <= 0) PSB_CUDA(cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, m->device));
+  m->sm_count = sm_count;
+  cudaStream_t st = nullptr;  // preprocessing is synchronous, like the reference constructor
+  const int kBlocks = 148 * 16;
+
+  DeviceArray<int> d_row_ptr(size_t(rows) + 1), d_col(nnz);
+  DeviceArray<float> d_val(nnz);
+  PSB_CUDA(cudaMemcpyAsync(d_row_ptr.get(), row_ptr, sizeof(int) * (size_t(rows) + 1), cudaMemcpyHostToDevice, st));
+  PSB_CUDA(cudaMemcpyAsync(d_col.get(), col_ind, sizeof(int) * size_t(nnz), cudaMemcpyHostToDevice, st));
+  PSB_CUDA(cudaMemcpyAsync(d_val.get(), sp_data, sizeof(float) * size_t(nnz), cudaMemcpyHostToDevice, st));
+
+  // --- Number of worksets (AnalyzeMatrix).
+  {
+    DeviceArray<unsigned long long> counts(kSizeClasses);
+    PSB_CUDA(cudaMemsetAsync(counts.get(), 0, sizeof(unsigned long long) * kSizeClasses, st));
+    workset_size_counts<<<grid_for(rows, 256, kBlocks), 256, 0, st>>>(d_row_ptr.get(), rows, counts.get());
+    PSB_LAUNCH_CHECK();
+    unsigned long long h[kSizeClasses];
+    PSB_CUDA(cudaMemcpy(h, counts.get(), sizeof(h), cudaMemcpyDeviceToHost));
+    const unsigned long long threshold = 8ULL * unsigned(sm_count) * 4ULL;
+    int S = 0;
+    unsigned long long groups = threshold + 1;
+    while (groups >= threshold) {
+      groups = S < kSizeClasses ? h[S] : 0;
+      ++S;
+    }
+    if (S > kMaxWorksets) throw std::runtime_error("too many worksets");
+    m->S = S;
+  }
+  const int S = m->S, fine = m->fine;
+
+  // --- Column frequencies.
+  DeviceArray<int> d_col_nnz(cols);
+  PSB_CUDA(cudaMemsetAsync(d_col_nnz.get(), 0, sizeof(int) * size_t(cols), st));
+  col_histogram<<<grid_for(nnz, 256, kBlocks), 256, 0, st>>>(d_col.get(), nnz, d_col_nnz.get());
+  PSB_LAUNCH_CHECK();
+  std::vector<int> h_col_nnz(cols);
+  PSB_CUDA(cudaMemcpy(h_col_nnz.data(), d_col_nnz.get(), sizeof(int) * size_t(cols), cudaMemcpyDeviceToHost));
+  const int maxcnt = *std::max_element(h_col_nnz.begin(), h_col_nnz.end());
+
+  // --- Within-row order: frequency descending, stable (thrust::sort of NNZPoint).
+  DeviceArray<uint32_t> perm;  // perm[i] = CSR position of the i-th element in frequency order
+  {
+    DeviceArray<uint64_t> keys(nnz), keys_alt(nnz);
+    DeviceArray<uint32_t> vals(nnz), vals_alt(nnz);
+    const int wc = bits_for(unsigned(maxcnt));
+    const int wr = bits_for(unsigned(rows - 1));
+    freq_sort_keys<<<grid_for(rows, 8, kBlocks), 256, 0, st>>>(d_row_ptr.get(), rows, d_col.get(),
+                                                               d_col_nnz.get(), maxcnt, wc, keys.get(),
+                                                               vals.get());
+    PSB_LAUNCH_CHECK();
+    const bool alt = radix_sort_pairs<uint64_t>(keys.get(), vals.get(), keys_alt.get(), vals_alt.get(),
+                                                size_t(nnz), 0, wc + wr, st);
+    perm = alt ? std::move(vals_alt) : std::move(vals);
+  }
+  d_col_nnz.release();
+
+  // --- Groups per workset and their source metadata.
+  DeviceArray<int> counts(size_t(S) * rows), prefix(size_t(S) * (size_t(rows) + 1));
+  row_group_counts<<<grid_for(rows, 256, kBlocks), 256, 0, st>>>(d_row_ptr.get(), rows, S, fine, counts.get());
+  PSB_LAUNCH_CHECK();
+  m->group_num.assign(S, 0);
+  for (int s = 0; s < S; ++s) {
+    int* pre = prefix.get() + size_t(s) * (size_t(rows) + 1);
+    exclusive_scan<int32_t>(counts.get() + size_t(s) * rows, pre, size_t(rows), st);
+    PSB_CUDA(cudaMemcpy(&m->group_num[s], pre + rows, sizeof(int), cudaMemcpyDeviceToHost));
+  }
+  counts.release();
+  const int G0 = m->group_num[0];
+  std::vector<DeviceArray<int>> src_des(S), src_start(S);
+  DeviceArray<int> res_size(G0);
+  DeviceArray<unsigned char> res_atomic_src(G0);
+  WorksetArrays wa{};
+  for (int s = 0; s < S; ++s) {
+    src_des[s].reset(m->group_num[s]);
+    src_start[s].reset(m->group_num[s]);
+    wa.des[s] = src_des[s].get();
+    wa.start[s] = src_start[s].get();
+    wa.groups[s] = m->group_num[s];
+  }
+  group_metadata<<<grid_for(rows, 256, kBlocks), 256, 0, st>>>(d_row_ptr.get(), rows, S, fine, prefix.get(), wa,
+                                                               res_size.get(), res_atomic_src.get());
+  PSB_LAUNCH_CHECK();
+
+  // --- Signatures (GenerateSigBit on the host, bits on the device).
+  std::vector<int> h_sigbit;
+  signature_bits(cols, h_col_nnz, h_sigbit, m->signature_len);
+  const int words = m->signature_len / 32;
+  DeviceArray<int> d_sigbit(cols);
+  PSB_CUDA(cudaMemcpy(d_sigbit.get(), h_sigbit.data(), sizeof(int) * size_t(cols), cudaMemcpyHostToDevice));
+  std::vector<DeviceArray<uint32_t>> sig(S);
+  for (int s = 0; s < S; ++s) {
+    sig[s].reset(size_t(words) * m->group_num[s]);
+    if (m->group_num[s])
+      PSB_CUDA(cudaMemsetAsync(sig[s].get(), 0, sizeof(uint32_t) * size_t(words) * m->group_num[s], st));
+    wa.sig[s] = sig[s].get();
+  }
+  group_signatures<<<grid_for(rows, 8, kBlocks), 256, 0, st>>>(d_row_ptr.get(), rows, S, fine, prefix.get(),
+                                                               perm.get(), d_col.get(), d_sigbit.get(), wa);
+  PSB_LAUNCH_CHECK();
+  prefix.release();
+  d_sigbit.release();
+
+  // --- Signature order of the groups of every workset: stable, lexicographically
+  // descending over words (LSD: last word first, as utils/matrix_utils.cu:590-592).
+  std::vector<DeviceArray<uint32_t>> order(S);
+  for (int s = 0; s < S; ++s) {
+    const int G = m->group_num[s];
+    order[s].reset(G);
+    if (!G) continue;
+    iota_u32(order[s].get(), G, st);
+    DeviceArray<uint32_t> keys(G), keys_alt(G), idx_alt(G);
+    uint32_t* idx = order[s].get();
+    uint32_t* idx2 = idx_alt.get();
+    for (int w = words - 1; w >= 0; --w) {
+      signature_word_keys<<<grid_for(G, 256, kBlocks), 256, 0, st>>>(sig[s].get() + size_t(w) * G, idx, G,
+                                                                     keys.get());
+      PSB_LAUNCH_CHECK();
+      if (radix_sort_pairs<uint32_t>(keys.get(), idx, keys_alt.get(), idx2, size_t(G), 0, 32, st))
+        std::swap(idx, idx2);
+    }
+    if (idx != order[s].get())
+      PSB_CUDA(cudaMemcpy(order[s].get(), idx, sizeof(uint32_t) * size_t(G), cudaMemcpyDeviceToDevice));
+    sig[s].release();
+  }
+
+  // --- Final worksets.
+  m->col_ind.assign(S, nullptr);
+  m->sp_data.assign(S, nullptr);
+  m->group_des.assign(S, nullptr);
+  m->ws_size.assign(S, 0);
+  DeviceArray<int> res_off(size_t(G0) + 1);
+  {
+    DeviceArray<int> size_perm(G0);
+    DeviceArray<bool> atomic_out(G0);
+    DeviceArray<int> des_out(G0);
+    if (G0) {
+      permute_residue_meta<<<grid_for(G0, 256, kBlocks), 256, 0, st>>>(order[0].get(), G0, res_size.get(),
+                                                                        res_atomic_src.get(), src_des[0].get(),
+                                                                        size_perm.get(), atomic_out.get(),
+                                                                        des_out.get());
+      PSB_LAUNCH_CHECK();
+    }
+    exclusive_scan<int32_t>(size_perm.get(), res_off.get(), size_t(G0), st);
+    m->residue_atomic = atomic_out.release_ownership();
+    m->group_des[0] = des_out.release_ownership();
+  }
+  std::vector<int> h_res_off(size_t(G0) + 1);
+  PSB_CUDA(cudaMemcpy(h_res_off.data(), res_off.get(), sizeof(int) * (size_t(G0) + 1), cudaMemcpyDeviceToHost));
+  const int wcol = bits_for(unsigned(cols - 1));
+  for (int s = 0; s < S; ++s) {
+    const int G = m->group_num[s];
+    const long long n = s == 0 ? (long long)h_res_off[G0] : (long long)G * group_size(s);
+    m->ws_size[s] = n;
+    if (s > 0 && G) {
+      DeviceArray<int> des_out(G);
+      permute_block_des<<<grid_for(G, 256, kBlocks), 256, 0, st>>>(order[s].get(), G, src_des[s].get(),
+                                                                   des_out.get());
+      PSB_LAUNCH_CHECK();
+      m->group_des[s] = des_out.release_ownership();
+    }
+    if (n == 0) continue;
+    DeviceArray<uint64_t> keys(n), keys_alt(n);
+    DeviceArray<uint32_t> vals(n), vals_alt(n);
+    gather_group_elements<<<grid_for(G, 8, kBlocks), 256, 0, st>>>(
+        order[s].get(), G, s == 0 ? 0 : group_size(s), s == 0 ? res_off.get() : nullptr,
+        s == 0 ? res_size.get() : nullptr, src_start[s].get(), perm.get(), d_col.get(), wcol, keys.get(),
+        vals.get());
+    PSB_LAUNCH_CHECK();
+    const int wg = bits_for(unsigned(G - 1));
+    const bool alt = radix_sort_pairs<uint64_t>(keys.get(), vals.get(), keys_alt.get(), vals_alt.get(),
+                                                size_t(n), 0, wcol + wg, st);
+    DeviceArray<int> col_out(n);
+    DeviceArray<float> val_out(n);
+    finalize_workset<<<grid_for(n, 256, kBlocks), 256, 0, st>>>(alt ? keys_alt.get() : keys.get(),
+                                                                alt ? vals_alt.get() : vals.get(), n,
+                                                                (uint64_t(1) << wcol) - 1, d_val.get(),
+                                                                col_out.get(), val_out.get());
+    PSB_LAUNCH_CHECK();
+    m->col_ind[s] = col_out.release_ownership();
+    m->sp_data[s] = val_out.release_ownership();
+  }
+  m->residue_offset = res_off.release_ownership();
+
+  // --- Tasks for the fused kernels.
+  const std::vector<Task> tasks = build_tasks(*m, h_res_off);
+  m->num_tasks = int(tasks.size());
+  if (!tasks.empty()) {
+    PSB_CUDA(cudaMalloc(reinterpret_cast<void**>(&m->tasks), sizeof(Task) * tasks.size()));
+    PSB_CUDA(cudaMemcpy(m->tasks, tasks.data(), sizeof(Task) * tasks.size(), cudaMemcpyHostToDevice));
+  }
+  PSB_CUDA(cudaDeviceSynchronize());
+  m->preprocess_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+  return m.release();
+}
+
+}  // namespace psb

@@ -1,0 +1,66 @@
+// The preprocessed matrix owned by the library (behind the opaque ps_matrix handle).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <vector>
+
+namespace psb {
+
+constexpr int kMaxWorksets = 32;
+constexpr int kFineGroupSize = 16;  // utils/matrix_utils.cu:56 of the reference
+
+// GROUP_SIZE(s) of the reference (utils/matrix_utils.h:8): 32 * 2^(s-1) for s >= 1.
+inline int group_size(int s) { return 32 << (s - 1); }
+
+// A unit of SpMM/SDDMM work: elements [begin, end) of workset `ws`, starting in
+// group `group`.  Residue tasks cover whole groups; block tasks cover whole
+// groups, or one slice of a group when the group is longer than a task.
+struct Task {
+  int ws;
+  int begin;
+  int end;
+  int group;
+};
+
+struct Matrix {
+  int device = 0;
+  int rows = 0, cols = 0, nnz = 0;
+  int S = 0;                     // GroupTypeNum(): worksets including the residue
+  int fine = kFineGroupSize;     // GroupFineSize()
+  int sm_count = 0;              // SM count the workset heuristic used
+  int signature_len = 32;
+  double preprocess_ms = 0.0;
+
+  // The reference-visible layout (utils/matrix_utils.h:30-40).
+  std::vector<int> group_num;          // host [S]
+  std::vector<int*> col_ind;           // device, per workset (nullptr when empty)
+  std::vector<float*> sp_data;         // device, per workset
+  std::vector<int*> group_des;         // device, per workset
+  std::vector<long long> ws_size;      // elements per workset
+  int* residue_offset = nullptr;       // device [G0 + 1]
+  bool* residue_atomic = nullptr;      // device [G0], nullptr when G0 == 0
+
+  // Work decomposition for the fused SpMM / SDDMM kernels (not part of the
+  // reference layout; derived from it).
+  Task* tasks = nullptr;               // device
+  int num_tasks = 0;
+
+  Matrix() = default;
+  Matrix(const Matrix&) = delete;
+  Matrix& operator=(const Matrix&) = delete;
+  ~Matrix();
+};
+
+// Builds the layout on the current device from host CSR.  Throws
+// std::invalid_argument on an invalid CSR (same checks and messages as
+// utils/matrix_utils.cu:475-488) and psb::CudaError on CUDA failures.
+// sm_count <= 0 uses the device's multiprocessor count.
+Matrix* build_matrix(int rows, int cols, int nnz, const int* row_ptr, const int* col_ind,
+                     const float* sp_data, int sm_count);
+
+// Task size in elements used by build_matrix.
+constexpr int kTaskElems = 256;
+
+}  // namespace psb
