@@ -1,0 +1,358 @@
+"""Benchmark of the PowerSparse hot path on B200: fused SpMM over the block/residue layout.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--n 128]
+
+One step = one SpMM call C = A·B (FP32) over one row panel per GPU.  Workload:
+benchmark configuration 2 (symmetric Chung-Lu power-law graph, gamma 2.1,
+2.45M nodes, ~61.9M nnz, values U[0,1], B U[-1,1], N = 128) per GPU; with N
+GPUs the graph has N x 2.45M nodes with the same degree law, is cut into N
+nnz-balanced row panels, and B (all N x 2.45M rows) is replicated (weak
+scaling; no collective in the timed region).  Inputs are larger than L2
+(B is 1.25 GB per 2.45M rows), so no explicit L2 flush is done.
+
+Prints one JSON line (rank 0).  ``--impl reference`` times the reference's CPU
+path (its FP64 CheckSpmm loop, benchmarks/benchmark.cu:64-77, restated in
+oracle/ps_oracle.cpp) on all host cores on the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "SpMM/SDDMM GFLOPS and HBM GB/s (% of roofline) at N=32/128, 1/2/4/8 B200"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def measured_peaks() -> tuple[float, str]:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def profile_traffic(kernel: str, workload: str):
+    """DRAM bytes per launch from a committed ncu summary, if one exists for this workload."""
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(p) as f:
+            return json.load(f)[kernel][workload]
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 50 ms while active."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.samples = []
+        self.proc = None
+        self.thread = None
+        self.window = [0.0, 0.0]
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "50",
+                 "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+            return self
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.samples.append((time.time(), line.strip()))
+
+    def stop(self):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=5)
+
+    def summary(self):
+        t0, t1 = self.window
+        rows = [s for t, s in self.samples if t0 - 0.06 <= t <= t1 + 0.06] or [s for _, s in self.samples]
+        mhz, maxmhz, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            f = [x.strip() for x in r.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                mhz.append(float(f[1]))
+                maxmhz.append(float(f[2]))
+            except ValueError:
+                continue
+            for name, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(name)
+        if not mhz:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": max(maxmhz), "reasons": sorted(reasons),
+                "samples": len(mhz)}
+
+
+def build_workload(rank: int, world: int, device):
+    import powersparse_b200 as psb
+    from powersparse_b200 import synth_gpu
+    n_nodes, pairs = synth_gpu.config2_pairs(nodes_scale=world, device=device)
+    cuts = psb.partition_rows(synth_gpu.global_row_ptr(pairs, n_nodes).astype(np.int32), world)
+    panel = synth_gpu.panel_from_pairs(pairs, n_nodes, int(cuts[rank]), int(cuts[rank + 1]), seed=2)
+    del pairs
+    return panel, cuts
+
+
+def dense_B(cols: int, n: int, device):
+    import torch
+    g = torch.Generator(device=device)
+    g.manual_seed(102)
+    return torch.rand((cols, n), generator=g, device=device, dtype=torch.float32) * 2 - 1
+
+
+def cpu_spmm_rate(panel, B_host: np.ndarray, min_seconds: float, max_passes: int):
+    """FP64 CheckSpmm restatement on all host cores; returns (GFLOP/s, threads, passes, seconds)."""
+    from oracle import oracle
+    threads = oracle.lib().ps_oracle_max_threads()
+    n = B_host.shape[1]
+    passes, t = 0, 0.0
+    while passes < max_passes and (passes == 0 or t < min_seconds):
+        t0 = time.perf_counter()
+        oracle.spmm(panel.row_ptr, panel.col_ind, panel.values, B_host, threads=threads)
+        t += time.perf_counter() - t0
+        passes += 1
+    flops = 2.0 * panel.nnz * n * passes
+    return flops / t / 1e9, threads, passes, t
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--n", type=int, default=128)
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=device)
+
+    N = args.n
+    if args.impl == "reference":
+        if rank == 0:
+            run_reference_arm(args, world, device)
+        if dist:
+            dist.destroy_process_group()
+        return
+
+    import powersparse_b200 as psb
+    panel, cuts = build_workload(rank, world, device)
+    m = psb.PowerSparseMatrixGPU(panel.rows, panel.cols, panel.nnz, panel.row_ptr, panel.col_ind, panel.values)
+    if rank == 0:
+        B = dense_B(panel.cols, N, device)
+    else:
+        B = torch.empty((panel.cols, N), dtype=torch.float32, device=device)
+    if dist:
+        dist.broadcast(B, 0)  # replicate the dense operand once (setup, untimed)
+    C = torch.zeros((panel.rows, N), dtype=torch.float32, device=device)
+    stream = torch.cuda.current_stream(device)
+
+    for _ in range(max(args.warmup, 3)):
+        psb.SpMM(m, N, B, C, stream)
+    torch.cuda.synchronize(device)
+
+    sampler = ClockSampler(local).start()
+    time.sleep(0.15)
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    sampler.window[0] = time.time()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        psb.SpMM(m, N, B, C, stream)
+    ev1.record(stream)
+    torch.cuda.synchronize(device)
+    sampler.window[1] = time.time()
+    if dist:
+        dist.barrier()
+    time.sleep(0.1)
+    sampler.stop()
+    ms_local = ev0.elapsed_time(ev1) / args.steps
+    ms = ms_local
+    nnz_total = panel.nnz
+    if dist:
+        t = torch.tensor([ms_local], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        z = torch.tensor([panel.nnz], dtype=torch.float64, device=device)
+        dist.all_reduce(z)
+        nnz_total = int(z.item())
+    gflops = 2.0 * nnz_total * N / (ms * 1e-3) / 1e9
+
+    # Roofline of the fused kernel (per GPU): compulsory bytes 8*nnz + 4*N*(rows + cols).
+    alg_bytes = 8.0 * panel.nnz + 4.0 * N * (panel.rows + panel.cols)
+    peak, peak_kind = measured_peaks()
+    achieved = alg_bytes / (ms_local * 1e-3) / 1e9
+    workload = f"cfg2_spmm_n{N}_x{world}"
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "peak_source": peak_kind,
+                "traffic": profile_traffic("spmm_fused", f"cfg2_spmm_n{N}"),
+                "alg_bytes_per_launch": alg_bytes}
+
+    # SpMM at N=32 on the same panel (kernel only, same timing rules).
+    extra = {}
+    if N != 32:
+        B32 = B[:, :32].contiguous()
+        C32 = torch.zeros((panel.rows, 32), dtype=torch.float32, device=device)
+        for _ in range(3):
+            psb.SpMM(m, 32, B32, C32, stream)
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+        ev0.record(stream)
+        k32 = max(10, args.steps)
+        for _ in range(k32):
+            psb.SpMM(m, 32, B32, C32, stream)
+        ev1.record(stream)
+        torch.cuda.synchronize(device)
+        ms32 = ev0.elapsed_time(ev1) / k32
+        if dist:
+            t = torch.tensor([ms32], dtype=torch.float64, device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms32 = float(t.item())
+        ab32 = 8.0 * panel.nnz + 4.0 * 32 * (panel.rows + panel.cols)
+        extra["spmm_n32"] = {"ms": round(ms32, 4), "gflops": round(2.0 * nnz_total * 32 / (ms32 * 1e-3) / 1e9, 1),
+                             "roofline_frac": round(ab32 / (ms32 * 1e-3) / 1e9 / peak, 4)}
+        del B32, C32
+
+    # End to end through the public API with host buffers: per step, copy B from pinned
+    # host memory, zero C, run SpMM, copy C back.
+    hB = B.cpu().pin_memory()
+    hC = torch.empty((panel.rows, N), dtype=torch.float32).pin_memory()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    dB = torch.empty_like(B)
+    dC = torch.empty_like(C)
+
+    def e2e_step():
+        dB.copy_(hB, non_blocking=True)
+        dC.zero_()
+        psb.SpMM(m, N, dB, dC, stream)
+        hC.copy_(dC, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize(device)
+    if dist:
+        dist.barrier()
+    e0.record(stream)
+    for _ in range(args.e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    e2e_ms = e0.elapsed_time(e1) / args.e2e_steps
+    if dist:
+        t = torch.tensor([e2e_ms], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e = {"value": round(2.0 * nnz_total * N / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GFLOP/s",
+           "h2d_bytes_per_step": int(hB.numel() * 4), "d2h_bytes_per_step": int(hC.numel() * 4),
+           "ms_per_step": round(e2e_ms, 3), "steps": args.e2e_steps}
+    assert np.allclose(hC[:4].numpy(), C[:4].cpu().numpy(), rtol=1e-4, atol=1e-4)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rate, threads, passes, secs = cpu_spmm_rate(panel, hB.numpy(), min_seconds=10.0, max_passes=40)
+        cpu = {"value": round(rate, 2), "unit": "GFLOP/s", "cores": threads, "kind": "port",
+               "sample": f"full cfg2 SpMM N={N} (FP64 CheckSpmm restatement, OpenMP), {passes} passes, {secs:.1f} s"}
+
+    if rank == 0:
+        clocks = sampler.summary()
+        line = {
+            "metric": METRIC, "value": round(gflops, 1), "unit": "GFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": f"cfg2: SpMM N={N}, symmetric Chung-Lu gamma=2.1, {world}x2.45M nodes, "
+                                   f"nnz-balanced row panel per GPU, B replicated",
+                       "rows_per_gpu": panel.rows, "cols": panel.cols, "nnz_per_gpu_rank0": panel.nnz,
+                       "nnz_total": nnz_total, "N": N, "S": m.GroupTypeNum(),
+                       "parallelism": f"row-panel x{world}", "l2": "inputs larger than L2 (B >= 1.25 GB), no flush",
+                       "preprocess_ms": round(m.preprocess_ms, 1)},
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps,
+            "clocks": clocks, "extra": extra,
+        }
+        print(json.dumps(line), flush=True)
+    m.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_reference_arm(args, world: int, device) -> None:
+    """The reference's CPU path (FP64 CheckSpmm, restated: no separately callable CPU
+    SpMM exists in the reference) on all host cores, on rank 0's panel of the same workload."""
+    panel, _ = build_workload(0, world, device)
+    N = args.n
+    B = dense_B(panel.cols, N, device).cpu().numpy()
+    from oracle import oracle
+    threads = oracle.lib().ps_oracle_max_threads()
+    for _ in range(min(args.warmup, 1)):
+        oracle.spmm(panel.row_ptr, panel.col_ind, panel.values, B, threads=threads)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        oracle.spmm(panel.row_ptr, panel.col_ind, panel.values, B, threads=threads)
+        times.append(time.perf_counter() - t0)
+        if sum(times) > 120:
+            break
+    ms = 1e3 * sum(times) / len(times)
+    v = 2.0 * panel.nnz * N / (ms * 1e-3) / 1e9
+    line = {"metric": METRIC, "value": round(v, 2), "unit": "GFLOP/s", "n_gpus": world, "steps": len(times),
+            "warmup": min(args.warmup, 1), "ms_per_step": round(ms, 2), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic", "impl": "reference",
+            "config": {"workload": f"cfg2: SpMM N={N}, rank-0 row panel of {world}x2.45M-node graph",
+                       "rows": panel.rows, "nnz": panel.nnz, "N": N},
+            "cpu_baseline": {"value": round(v, 2), "unit": "GFLOP/s", "cores": threads, "kind": "port",
+                             "sample": f"one row panel ({panel.nnz} nnz) per step, FP64 CheckSpmm restatement"},
+            "e2e": {"value": round(v, 2), "unit": "GFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

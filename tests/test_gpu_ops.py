@@ -1,0 +1,158 @@
+"""GPU tests: fused SpMM / SDDMM against the FP64 oracle and the reference's outputs.
+
+Tolerance (the north star's): |a - e| <= 1e-5 + 1e-4 * |e| for every element,
+e the FP64 oracle value (the reference's CheckSpmm / CheckSddmm,
+benchmarks/benchmark.cu:64-96, at tighter constants).
+"""
+import numpy as np
+import pytest
+import torch
+
+import powersparse_b200 as psb
+from helpers import ATOL, RTOL, dense_inputs, golden_names, load_golden
+from oracle import oracle
+from powersparse_b200 import synth
+
+pytestmark = pytest.mark.gpu
+
+
+def _assert_close(actual, expected, tag=""):
+    ok = oracle.close(actual, expected, ATOL, RTOL)
+    if not ok.all():
+        bad = np.argwhere(~ok.reshape(-1))[:5].ravel()
+        a, e = np.asarray(actual).reshape(-1), np.asarray(expected).reshape(-1)
+        raise AssertionError(f"{tag}: {int((~ok).sum())} of {ok.size} outside tolerance; "
+                             f"first {[(int(i), float(a[i]), float(e[i])) for i in bad]}")
+
+
+def _spmm(m, B: np.ndarray, stream=None, C0=None):
+    N = B.shape[1]
+    dB = torch.from_numpy(B).cuda()
+    dC = torch.zeros((m.MatrixRow(), N), dtype=torch.float32, device="cuda") if C0 is None else C0
+    psb.SpMM(m, N, dB, dC, stream)
+    torch.cuda.synchronize()
+    return dC
+
+
+def _sddmm(m, X: np.ndarray, Y: np.ndarray):
+    N = X.shape[1]
+    outs = [torch.zeros(max(m.workset_size(s), 1), dtype=torch.float32, device="cuda")
+            for s in range(m.GroupTypeNum())]
+    psb.SDDMM(m, N, torch.from_numpy(X).cuda(), torch.from_numpy(Y).cuda(), outs)
+    torch.cuda.synchronize()
+    return [o[: m.workset_size(s)].cpu().numpy() for s, o in enumerate(outs)]
+
+
+@pytest.mark.parametrize("name", golden_names())
+def test_spmm_matches_oracle_and_reference(name):
+    z, rows, cols, rp, ci, va, sm = load_golden(name)
+    with psb.PowerSparseMatrixGPU(rows, cols, len(ci), rp, ci, va, sm_count=sm) as m:
+        for n in (32, 64, 96, 128, 256):
+            B = dense_inputs(cols, n, 1000 + n)
+            C = _spmm(m, B).cpu().numpy()
+            _assert_close(C, oracle.spmm(rp, ci, va, B), f"{name} N={n}")
+            key = f"spmm{n}"
+            if key in z.files:
+                assert oracle.close(C, z[key], 1e-4, 1e-4).all()
+            if key + "_head" in z.files:
+                assert oracle.close(C[: len(z[key + "_head"])], z[key + "_head"], 1e-4, 1e-4).all()
+
+
+@pytest.mark.parametrize("name", golden_names())
+def test_sddmm_matches_oracle_and_reference(name):
+    z, rows, cols, rp, ci, va, sm = load_golden(name)
+    L = oracle.build_layout(rows, cols, rp, ci, va, sm)
+    with psb.PowerSparseMatrixGPU(rows, cols, len(ci), rp, ci, va, sm_count=sm) as m:
+        for n in (32, 128):
+            X, Y = dense_inputs(rows, n, 2000 + n), dense_inputs(cols, n, 3000 + n)
+            got = _sddmm(m, X, Y)
+            exp = oracle.sddmm(L, X, Y)
+            for s in range(L.S):
+                _assert_close(got[s], exp[s], f"{name} N={n} ws{s}")
+                key = f"sddmm{n}_ws{s}"
+                if key in z.files:
+                    assert oracle.close(got[s], z[key], 1e-4, 1e-4).all()
+
+
+@pytest.mark.parametrize("cfg,scale", [(2, 0.004), (3, 0.004), (4, 0.01)])
+@pytest.mark.parametrize("sm", [1, 148])
+def test_ops_on_scaled_configs(cfg, scale, sm):
+    mtx = synth.config_matrix(cfg, scale=scale)
+    with psb.PowerSparseMatrixGPU(mtx.rows, mtx.cols, mtx.nnz, mtx.row_ptr, mtx.col_ind, mtx.values,
+                                  sm_count=sm) as m:
+        for n in (32, 128):
+            B = synth.dense(mtx.cols, n, 100 + cfg)
+            _assert_close(_spmm(m, B).cpu().numpy(), oracle.spmm(mtx.row_ptr, mtx.col_ind, mtx.values, B),
+                          f"cfg{cfg} spmm N={n}")
+        L = oracle.build_layout(mtx.rows, mtx.cols, mtx.row_ptr, mtx.col_ind, mtx.values, sm)
+        for n in (32, 128):
+            X, Y = synth.dense(mtx.rows, n, 200 + cfg), synth.dense(mtx.cols, n, 300 + cfg)
+            got, exp = _sddmm(m, X, Y), oracle.sddmm(L, X, Y)
+            for s in range(L.S):
+                _assert_close(got[s], exp[s], f"cfg{cfg} sddmm N={n} ws{s}")
+
+
+def test_spmm_accumulates_like_the_reference_when_not_zeroed():
+    """Rows whose groups add atomically accumulate; single-group residue rows are stored
+    (spmm_kernel_residue.cu:68-81), so a second call without zeroing doubles only the former."""
+    mtx = synth.chung_lu(3000, 14, 600, 2.1, seed=7)
+    L = oracle.build_layout(mtx.rows, mtx.cols, mtx.row_ptr, mtx.col_ind, mtx.values, 1)
+    stored = np.zeros(mtx.rows, dtype=bool)
+    for g in range(L.group_num[0]):
+        if not L.residue_atomic[g]:
+            stored[L.group_des[0][g]] = True
+    with psb.PowerSparseMatrixGPU(mtx.rows, mtx.cols, mtx.nnz, mtx.row_ptr, mtx.col_ind, mtx.values,
+                                  sm_count=1) as m:
+        B = dense_inputs(mtx.cols, 32, 5)
+        C = _spmm(m, B)
+        once = C.cpu().numpy().copy()
+        psb.SpMM(m, 32, torch.from_numpy(B).cuda(), C)
+        torch.cuda.synchronize()
+        twice = C.cpu().numpy()
+    assert stored.any() and (~stored).any()
+    _assert_close(twice[stored], once[stored], "stored rows")
+    _assert_close(twice[~stored], 2 * once[~stored].astype(np.float64), "atomic rows")
+
+
+def test_spmm_on_a_side_stream():
+    mtx = synth.chung_lu(2000, 20, 400, 2.1, seed=12)
+    with psb.PowerSparseMatrixGPU(mtx.rows, mtx.cols, mtx.nnz, mtx.row_ptr, mtx.col_ind, mtx.values,
+                                  sm_count=2) as m:
+        B = dense_inputs(mtx.cols, 128, 6)
+        s = torch.cuda.Stream()
+        dB = torch.from_numpy(B).cuda()
+        dC = torch.zeros((mtx.rows, 128), device="cuda")
+        torch.cuda.synchronize()
+        psb.SpMM(m, 128, dB, dC, s)
+        s.synchronize()
+        _assert_close(dC.cpu().numpy(), oracle.spmm(mtx.row_ptr, mtx.col_ind, mtx.values, B), "side stream")
+
+
+def test_operator_errors_match_the_reference():
+    mtx = synth.chung_lu(500, 10, 100, 2.1, seed=13)
+    with psb.PowerSparseMatrixGPU(mtx.rows, mtx.cols, mtx.nnz, mtx.row_ptr, mtx.col_ind, mtx.values) as m:
+        B = torch.zeros((mtx.cols, 64), device="cuda")
+        C = torch.zeros((mtx.rows, 64), device="cuda")
+        with pytest.raises(ValueError, match="positive multiple of 32"):
+            psb.SpMM(m, 48, B, C)
+        with pytest.raises(ValueError, match="positive multiple of 32"):
+            psb.SpMM(m, 0, B, C)
+        with pytest.raises(ValueError, match="Invalid SpMM buffers"):
+            psb.SpMM(m, 64, 0, C)
+        outs = [torch.zeros(max(m.workset_size(s), 1), device="cuda") for s in range(m.GroupTypeNum())]
+        with pytest.raises(ValueError, match="N=32 or N=128"):
+            psb.SDDMM(m, 64, B, B, outs)
+        bad = list(outs)
+        bad[0] = 0
+        with pytest.raises(ValueError, match="Missing SDDMM output workset"):
+            psb.SDDMM(m, 32, torch.zeros((mtx.rows, 32), device="cuda"), torch.zeros((mtx.cols, 32), device="cuda"),
+                      bad)
+
+
+def test_spmm_large_n_uses_several_slabs():
+    mtx = synth.chung_lu(1500, 16, 300, 2.1, seed=14)
+    with psb.PowerSparseMatrixGPU(mtx.rows, mtx.cols, mtx.nnz, mtx.row_ptr, mtx.col_ind, mtx.values,
+                                  sm_count=1) as m:
+        for n in (160, 384, 1024):
+            B = dense_inputs(mtx.cols, n, n)
+            _assert_close(_spmm(m, B).cpu().numpy(), oracle.spmm(mtx.row_ptr, mtx.col_ind, mtx.values, B), f"N={n}")
