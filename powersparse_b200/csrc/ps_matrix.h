@@ -44,7 +44,7 @@ struct Matrix {
 
   // Work decomposition for the fused SpMM / SDDMM kernels (not part of the
   // reference layout; derived from it).
-  Task* tasks = nullptr;               // device
+  Task* tasks = nullptr;               // device: block tasks (largest groups first), then residue
   int num_tasks = 0;
 
   Matrix() = default;

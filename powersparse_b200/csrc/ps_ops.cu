@@ -3,14 +3,22 @@
 // The reference launches one kernel per workset on its own stream and
 // device-synchronizes (PowerSparse_SpMM/spmm_solution.cu:16-33,
 // PowerSparse_SDDMM/sddmm_solution.cu:23-49).  Here one launch covers every
-// workset: the matrix carries a task list (ps_matrix.h) and each warp runs one
-// task, a contiguous element range of one workset, largest groups first.
+// workset: the matrix carries a task list (ps_matrix.h: about kTaskElems
+// elements per task, largest groups first) and each lane group runs one task.
 //
-// Lane layout: a warp owns a slab of 32*VEC consecutive columns of the dense
-// operand and handles one sparse element at a time, so every gathered dense row
-// segment is one fully coalesced 128*VEC-byte load (float4 per lane at N=128).
-// Column indices and values are staged per warp in shared memory 32 at a time
-// and read back as broadcasts.
+// Lane groups: LG lanes (8, 16 or 32) handle one sparse element at a time, each
+// lane owning 4 consecutive dense columns, so a gathered dense row segment of
+// 4*LG floats is one fully coalesced 16*LG-byte load.  A warp holds 32/LG lane
+// groups working on different tasks (at N = 32: four elements per warp
+// instruction, like the reference's 8-lane "octets").  Column indices and values
+// are staged 32 at a time per lane group in shared memory and read back as
+// broadcasts; gathers are issued kUnroll at a time.
+//
+// Design note, from measurements on B200 (configurations 2 and 4): the gathers
+// are latency-bound, and the number of warps per SM matters more than the depth
+// of each warp's load batch, so the kernels are written to stay near 56-64
+// registers (4 CTAs of 256 threads per SM) with kUnroll = 4.  The residue and
+// block paths are separate code regions so their registers do not add up.
 #include "ps_common.cuh"
 #include "ps_matrix.h"
 #include "ps_ops.h"
@@ -20,51 +28,32 @@ namespace {
 
 constexpr int kWarpsPerBlock = 8;
 constexpr int kThreads = kWarpsPerBlock * 32;
+constexpr int kChunk = 32;   // staged elements per lane group
+constexpr int kUnroll = 4;   // gathers in flight per lane group
+static_assert(kChunk % kUnroll == 0, "kUnroll must divide the staged chunk");
 
 struct WorksetView {
   const int* col[kMaxWorksets];
   const float* val[kMaxWorksets];
   const int* des[kMaxWorksets];
+  int group_len[kMaxWorksets];
+  int groups[kMaxWorksets];
 };
 
-template <int VEC> struct VecT;
-template <> struct VecT<1> { using T = float; };
-template <> struct VecT<2> { using T = float2; };
-template <> struct VecT<4> { using T = float4; };
-
-template <int VEC>
-__device__ __forceinline__ void load_vec(const float* __restrict__ p, float (&v)[VEC]) {
-  if constexpr (VEC == 4) {
-    const float4 x = __ldg(reinterpret_cast<const float4*>(p));
-    v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
-  } else if constexpr (VEC == 2) {
-    const float2 x = __ldg(reinterpret_cast<const float2*>(p));
-    v[0] = x.x; v[1] = x.y;
-  } else {
-    v[0] = __ldg(p);
-  }
+__device__ __forceinline__ void fma4(float4& acc, float s, const float4& b) {
+  acc.x = fmaf(s, b.x, acc.x);
+  acc.y = fmaf(s, b.y, acc.y);
+  acc.z = fmaf(s, b.z, acc.z);
+  acc.w = fmaf(s, b.w, acc.w);
 }
 
-// Adds (atomic) or stores one lane's VEC outputs.
-template <int VEC>
-__device__ __forceinline__ void emit(float* __restrict__ dst, const float (&v)[VEC], bool atomic) {
-  if (atomic) {
-    if constexpr (VEC == 4) {
-      atomicAdd(reinterpret_cast<float4*>(dst), make_float4(v[0], v[1], v[2], v[3]));
-    } else if constexpr (VEC == 2) {
-      atomicAdd(reinterpret_cast<float2*>(dst), make_float2(v[0], v[1]));
-    } else {
-      atomicAdd(dst, v[0]);
-    }
-  } else {
-    if constexpr (VEC == 4) {
-      *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
-    } else if constexpr (VEC == 2) {
-      *reinterpret_cast<float2*>(dst) = make_float2(v[0], v[1]);
-    } else {
-      *dst = v[0];
-    }
-  }
+__device__ __forceinline__ float dot4(const float4& a, const float4& b) {
+  return fmaf(a.w, b.w, fmaf(a.z, b.z, fmaf(a.y, b.y, a.x * b.x)));
+}
+
+__device__ __forceinline__ void emit4(float* dst, const float4& v, bool atomic) {
+  if (atomic) atomicAdd(reinterpret_cast<float4*>(dst), v);
+  else __stcs(reinterpret_cast<float4*>(dst), v);
 }
 
 struct SpmmArgs {
@@ -77,136 +66,120 @@ struct SpmmArgs {
   const float* B;
   float* C;
   long long ldb;  // N
-  int group_len[kMaxWorksets];
 };
 
-// SpMM: C[row(g), :] (+)= sum over elements e of group g of val[e] * B[col[e], :].
+// SpMM, one task per lane group:
+//   C[row(g), slab] (+)= sum over elements e of group g of val[e] * B[col[e], slab].
 // Block groups always add atomically and residue groups add atomically only when
 // their row has other groups, as in spmm_kernel_block.cu:155-161 and
 // spmm_kernel_residue.cu:68-81 of the reference.  Block groups accumulate FP32
 // per 32-element chunk and carry the running sum in FP64.
-template <int VEC, int UNROLL>
+template <int LG>
 __global__ void __launch_bounds__(kThreads) spmm_fused(const SpmmArgs a) {
-  __shared__ int s_col[kWarpsPerBlock][32];
-  __shared__ float s_val[kWarpsPerBlock][32];
+  constexpr int NG = 32 / LG;
+  __shared__ int s_col[kWarpsPerBlock][NG][kChunk + 1];
+  __shared__ float s_val[kWarpsPerBlock][NG][kChunk + 1];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int task_id = blockIdx.x * kWarpsPerBlock + warp;
+  const int q = lane / LG, l = lane % LG;
+  const unsigned gm = LG == 32 ? 0xffffffffu : (((1u << LG) - 1u) << (q * LG));
+  const int task_id = (blockIdx.x * kWarpsPerBlock + warp) * NG + q;
   if (task_id >= a.num_tasks) return;
   const Task t = a.tasks[task_id];
   const int* __restrict__ col = a.ws.col[t.ws];
   const float* __restrict__ val = a.ws.val[t.ws];
   const int* __restrict__ des = a.ws.des[t.ws];
-  const long long colofs = (long long)blockIdx.y * (32 * VEC) + lane * VEC;
+  const int colofs = blockIdx.y * (4 * LG) + l * 4;
   const float* __restrict__ Bl = a.B + colofs;
   float* __restrict__ Cl = a.C + colofs;
-  int* sc = s_col[warp];
-  float* sv = s_val[warp];
-
-  float acc[VEC];
+  int* sc = s_col[warp][q];
+  float* sv = s_val[warp][q];
+  auto stage = [&](int base, int n) {
 #pragma unroll
-  for (int v = 0; v < VEC; ++v) acc[v] = 0.f;
-
-  if (t.ws == 0) {
-    // Residue: groups of <= 31 elements, boundaries from the residue offsets.
-    // Lane i holds the metadata of group (wbase + i); it is read by shuffles.
-    int wbase = t.group;
-    int g_end = 0, g_row = 0, g_atomic = 0;
-    {
-      const int gi = wbase + lane;
-      if (gi < a.res_groups) {
-        g_end = a.res_off[gi + 1];
-        g_row = des[gi];
-        g_atomic = a.res_atomic[gi];
+    for (int r = 0; r < kChunk / LG; ++r) {
+      const int i = l + r * LG;
+      if (i < n) {
+        sc[i] = __ldcs(col + base + i);
+        sv[i] = __ldcs(val + base + i);
       }
     }
+  };
+  auto gather = [&](int c) { return __ldg(reinterpret_cast<const float4*>(Bl + (long long)c * a.ldb)); };
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+
+  if (t.ws == 0) {
+    // Residue: groups of <= 31 elements; lane l holds the metadata of group wbase + l.
+    int wbase = t.group;
+    int g_end = 0, g_row = 0, g_atomic = 0;
+    if (wbase + l < a.res_groups) {
+      g_end = a.res_off[wbase + l + 1];
+      g_row = des[wbase + l];
+      g_atomic = a.res_atomic[wbase + l];
+    }
     int widx = 0;
-    int cur_end = __shfl_sync(0xffffffffu, g_end, 0);
-    int cur_row = __shfl_sync(0xffffffffu, g_row, 0);
-    bool cur_atomic = __shfl_sync(0xffffffffu, g_atomic, 0);
-    for (int base = t.begin; base < t.end; base += 32) {
-      const int n = min(32, t.end - base);
-      if (lane < n) {
-        sc[lane] = __ldcs(col + base + lane);
-        sv[lane] = __ldcs(val + base + lane);
-      }
-      __syncwarp();
-      for (int j = 0; j < n; j += UNROLL) {
-        float b[UNROLL][VEC];
+    int cur_end = __shfl_sync(gm, g_end, 0, LG);
+    int cur_row = __shfl_sync(gm, g_row, 0, LG);
+    bool cur_atomic = __shfl_sync(gm, g_atomic, 0, LG);
+    for (int base = t.begin; base < t.end; base += kChunk) {
+      const int n = min(kChunk, t.end - base);
+      stage(base, n);
+      __syncwarp(gm);
+      for (int j = 0; j < n; j += kUnroll) {
+        float4 b[kUnroll];
 #pragma unroll
-        for (int u = 0; u < UNROLL; ++u) {
-          if (j + u < n) load_vec<VEC>(Bl + (long long)sc[j + u] * a.ldb, b[u]);
-        }
+        for (int u = 0; u < kUnroll; ++u)
+          if (j + u < n) b[u] = gather(sc[j + u]);
 #pragma unroll
-        for (int u = 0; u < UNROLL; ++u) {
+        for (int u = 0; u < kUnroll; ++u) {
           if (j + u < n) {
-            const int pos = base + j + u;
-            if (pos == cur_end) {
-              emit<VEC>(Cl + (long long)cur_row * a.ldb, acc, cur_atomic);
-#pragma unroll
-              for (int v = 0; v < VEC; ++v) acc[v] = 0.f;
-              if (++widx == 32) {
-                wbase += 32;
+            if (base + j + u == cur_end) {
+              emit4(Cl + (long long)cur_row * a.ldb, acc, cur_atomic);
+              acc = make_float4(0.f, 0.f, 0.f, 0.f);
+              if (++widx == LG) {
+                wbase += LG;
                 widx = 0;
-                const int gi = wbase + lane;
-                if (gi < a.res_groups) {
-                  g_end = a.res_off[gi + 1];
-                  g_row = des[gi];
-                  g_atomic = a.res_atomic[gi];
+                if (wbase + l < a.res_groups) {
+                  g_end = a.res_off[wbase + l + 1];
+                  g_row = des[wbase + l];
+                  g_atomic = a.res_atomic[wbase + l];
                 }
               }
-              cur_end = __shfl_sync(0xffffffffu, g_end, widx);
-              cur_row = __shfl_sync(0xffffffffu, g_row, widx);
-              cur_atomic = __shfl_sync(0xffffffffu, g_atomic, widx);
+              cur_end = __shfl_sync(gm, g_end, widx, LG);
+              cur_row = __shfl_sync(gm, g_row, widx, LG);
+              cur_atomic = __shfl_sync(gm, g_atomic, widx, LG);
             }
-            const float s = sv[j + u];
-#pragma unroll
-            for (int v = 0; v < VEC; ++v) acc[v] = fmaf(s, b[u][v], acc[v]);
+            fma4(acc, sv[j + u], b[u]);
           }
         }
       }
-      __syncwarp();
+      __syncwarp(gm);
     }
-    emit<VEC>(Cl + (long long)cur_row * a.ldb, acc, cur_atomic);
+    emit4(Cl + (long long)cur_row * a.ldb, acc, cur_atomic);
     return;
   }
 
-  // Block workset: every group has group_len elements, all added atomically.
-  const int G = a.group_len[t.ws];
+  // Block workset: groups of group_len (a multiple of 32) elements; a task is a
+  // whole number of 32-element chunks inside one group or a run of whole groups.
+  const int G = a.ws.group_len[t.ws];
   int g = t.group;
-  double accd[VEC];
-#pragma unroll
-  for (int v = 0; v < VEC; ++v) accd[v] = 0.0;
-  for (int base = t.begin; base < t.end; base += 32) {
-    sc[lane] = __ldcs(col + base + lane);
-    sv[lane] = __ldcs(val + base + lane);
-    __syncwarp();
+  double dx = 0.0, dy = 0.0, dz = 0.0, dw = 0.0;
+  for (int base = t.begin; base < t.end; base += kChunk) {
+    stage(base, kChunk);
+    __syncwarp(gm);
 #pragma unroll 1
-    for (int j = 0; j < 32; j += UNROLL) {
-      float b[UNROLL][VEC];
+    for (int j = 0; j < kChunk; j += kUnroll) {
+      float4 b[kUnroll];
 #pragma unroll
-      for (int u = 0; u < UNROLL; ++u) load_vec<VEC>(Bl + (long long)sc[j + u] * a.ldb, b[u]);
+      for (int u = 0; u < kUnroll; ++u) b[u] = gather(sc[j + u]);
 #pragma unroll
-      for (int u = 0; u < UNROLL; ++u) {
-        const float s = sv[j + u];
-#pragma unroll
-        for (int v = 0; v < VEC; ++v) acc[v] = fmaf(s, b[u][v], acc[v]);
-      }
+      for (int u = 0; u < kUnroll; ++u) fma4(acc, sv[j + u], b[u]);
     }
-    __syncwarp();
-#pragma unroll
-    for (int v = 0; v < VEC; ++v) {
-      accd[v] += double(acc[v]);
-      acc[v] = 0.f;
-    }
-    const int next = base + 32;
+    __syncwarp(gm);
+    dx += acc.x; dy += acc.y; dz += acc.z; dw += acc.w;
+    acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    const int next = base + kChunk;
     if (next == t.end || next % G == 0) {
-      float out[VEC];
-#pragma unroll
-      for (int v = 0; v < VEC; ++v) {
-        out[v] = float(accd[v]);
-        accd[v] = 0.0;
-      }
-      emit<VEC>(Cl + (long long)des[g] * a.ldb, out, true);
+      emit4(Cl + (long long)des[g] * a.ldb, make_float4(float(dx), float(dy), float(dz), float(dw)), true);
+      dx = dy = dz = dw = 0.0;
       ++g;
     }
   }
@@ -217,108 +190,132 @@ struct SddmmArgs {
   const Task* tasks;
   int num_tasks;
   const int* res_off;
+  int res_groups;
   const float* lhs;
   const float* rhs;
   float* out_ws[kMaxWorksets];
-  int group_len[kMaxWorksets];
 };
 
-// Reduces 32 per-lane partial sums (one per element) across the warp so that lane
-// l ends with the full sum of element l: halve the element set each step, keep
-// the half selected by the lane bit, add the partner's copy of it (31 shuffles).
-__device__ __forceinline__ float transpose_reduce32(float (&p)[32], int lane) {
+// Reduces kUnroll (= 4) per-lane partial dot products over the LG lanes of a lane
+// group.  Two halving steps on the top two lane bits leave lane l with element
+// (l / (LG / 4)) summed over 4 lanes; butterfly steps on the lower bits finish
+// the sum.
+template <int LG>
+__device__ __forceinline__ float reduce4(float (&p)[4], int l, unsigned gm) {
 #pragma unroll
-  for (int k = 16; k >= 1; k >>= 1) {
-    const bool upper = lane & k;
+  for (int h = 2, bit = LG / 2; h >= 1; h >>= 1, bit >>= 1) {
+    const bool upper = l & bit;
 #pragma unroll
-    for (int i = 0; i < k; ++i) {
-      const float send = upper ? p[i] : p[i + k];
-      const float keep = upper ? p[i + k] : p[i];
-      p[i] = keep + __shfl_xor_sync(0xffffffffu, send, k);
+    for (int i = 0; i < h; ++i) {
+      const float send = upper ? p[i] : p[i + h];
+      const float keep = upper ? p[i + h] : p[i];
+      p[i] = keep + __shfl_xor_sync(gm, send, bit, LG);
     }
   }
-  return p[0];
+  float v = p[0];
+#pragma unroll
+  for (int bit = LG / 8; bit >= 1; bit >>= 1) v += __shfl_xor_sync(gm, v, bit, LG);
+  return v;
 }
 
-// SDDMM: out[e] (+)= val[e] * <lhs[row(g)], rhs[col[e]]> for every element e of
-// group g, N = 32 * VEC.  Block outputs are stored (sddmm_kernel_block.cu:160-164);
-// residue outputs are added, matching the reference's atomicAdd into a zeroed
-// buffer (sddmm_kernel_residue.cu:297-305).
-template <int VEC, int UNROLL>
+// SDDMM, one task per lane group, N = 4 * LG:
+//   out[e] (+)= val[e] * <lhs[row(g)], rhs[col[e]]>.
+// Block outputs are stored (sddmm_kernel_block.cu:160-164 of the reference);
+// residue outputs are added, as its residue kernels atomically add into a
+// zeroed buffer (sddmm_kernel_residue.cu:297-305).
+template <int LG>
 __global__ void __launch_bounds__(kThreads) sddmm_fused(const SddmmArgs a) {
-  __shared__ int s_col[kWarpsPerBlock][32];
+  static_assert(kUnroll == 4, "reduce4 reduces four elements");
+  constexpr int NG = 32 / LG;
+  constexpr int kLanesPerElem = LG / 4;
+  __shared__ int s_col[kWarpsPerBlock][NG][kChunk + 1];
+  __shared__ float s_val[kWarpsPerBlock][NG][kChunk + 1];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int task_id = blockIdx.x * kWarpsPerBlock + warp;
+  const int q = lane / LG, l = lane % LG;
+  const unsigned gm = LG == 32 ? 0xffffffffu : (((1u << LG) - 1u) << (q * LG));
+  const int task_id = (blockIdx.x * kWarpsPerBlock + warp) * NG + q;
   if (task_id >= a.num_tasks) return;
   const Task t = a.tasks[task_id];
   const int* __restrict__ col = a.ws.col[t.ws];
   const float* __restrict__ val = a.ws.val[t.ws];
   const int* __restrict__ des = a.ws.des[t.ws];
   float* __restrict__ out = a.out_ws[t.ws];
-  const long long N = 32 * VEC;
-  const float* __restrict__ rhs_l = a.rhs + lane * VEC;
-  const float* __restrict__ lhs_l = a.lhs + lane * VEC;
-  int* sc = s_col[warp];
+  const long long N = 4 * LG;
+  const float* __restrict__ rhs_l = a.rhs + 4 * l;
+  const float* __restrict__ lhs_l = a.lhs + 4 * l;
+  int* sc = s_col[warp][q];
+  float* sv = s_val[warp][q];
   const bool residue = t.ws == 0;
-  const int G = residue ? 0 : a.group_len[t.ws];
+  const int G = a.ws.group_len[t.ws];
+  auto lhs_row = [&](int gi) { return __ldg(reinterpret_cast<const float4*>(lhs_l + (long long)des[gi] * N)); };
 
   int g = t.group;
   int cur_end = residue ? a.res_off[g + 1] : (g + 1) * G;
-  float x[VEC];
-  load_vec<VEC>(lhs_l + (long long)des[g] * N, x);
-
-  for (int base = t.begin; base < t.end; base += 32) {
-    const int n = min(32, t.end - base);
-    const float my_val = lane < n ? __ldcs(val + base + lane) : 0.f;
-    if (lane < n) sc[lane] = __ldcs(col + base + lane);
-    __syncwarp();
-    float p[32];
+  float4 x = lhs_row(g);
+  for (int base = t.begin; base < t.end; base += kChunk) {
+    const int n = min(kChunk, t.end - base);
 #pragma unroll
-    for (int j0 = 0; j0 < 32; j0 += UNROLL) {
-      float y[UNROLL][VEC];
-#pragma unroll
-      for (int u = 0; u < UNROLL; ++u) {
-        if (j0 + u < n) load_vec<VEC>(rhs_l + (long long)sc[j0 + u] * N, y[u]);
+    for (int r = 0; r < kChunk / LG; ++r) {
+      const int i = l + r * LG;
+      if (i < n) {
+        sc[i] = __ldcs(col + base + i);
+        sv[i] = __ldcs(val + base + i);
       }
+    }
+    __syncwarp(gm);
+    for (int j = 0; j < n; j += kUnroll) {
+      float4 y[kUnroll];
 #pragma unroll
-      for (int u = 0; u < UNROLL; ++u) {
-        const int j = j0 + u;
-        float d = 0.f;
-        if (j < n) {
-          if (base + j == cur_end) {
+      for (int u = 0; u < kUnroll; ++u)
+        if (j + u < n) y[u] = __ldg(reinterpret_cast<const float4*>(rhs_l + (long long)sc[j + u] * N));
+      float p[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        p[u] = 0.f;
+        if (j + u < n) {
+          if (base + j + u == cur_end) {
             ++g;
             cur_end = residue ? a.res_off[g + 1] : (g + 1) * G;
-            load_vec<VEC>(lhs_l + (long long)des[g] * N, x);
+            x = lhs_row(g);
           }
-#pragma unroll
-          for (int v = 0; v < VEC; ++v) d = fmaf(x[v], y[u][v], d);
+          p[u] = dot4(x, y[u]);
         }
-        p[j] = d;
+      }
+      const float dot = reduce4<LG>(p, l, gm);
+      const int jl = j + l / kLanesPerElem;
+      if (l % kLanesPerElem == 0 && jl < n) {
+        const float r = dot * sv[jl];
+        if (residue) atomicAdd(out + base + jl, r);
+        else out[base + jl] = r;
       }
     }
-    const float dot = transpose_reduce32(p, lane);
-    if (lane < n) {
-      const float r = dot * my_val;
-      if (residue) atomicAdd(out + base + lane, r);
-      else out[base + lane] = r;
-    }
-    __syncwarp();
+    __syncwarp(gm);
   }
 }
 
-unsigned task_blocks(int num_tasks) { return unsigned((num_tasks + kWarpsPerBlock - 1) / kWarpsPerBlock); }
+unsigned task_blocks(int num_tasks, int lane_group) {
+  const long long per_block = (long long)kWarpsPerBlock * (32 / lane_group);
+  return unsigned((num_tasks + per_block - 1) / per_block);
+}
+
+WorksetView view_of(const Matrix& m) {
+  WorksetView v{};
+  for (int s = 0; s < m.S; ++s) {
+    v.col[s] = m.col_ind[s];
+    v.val[s] = m.sp_data[s];
+    v.des[s] = m.group_des[s];
+    v.group_len[s] = s == 0 ? 0 : group_size(s);
+    v.groups[s] = m.group_num[s];
+  }
+  return v;
+}
 
 }  // namespace
 
 void spmm_launch(const Matrix& m, int N, const float* B, float* C, cudaStream_t stream) {
   if (m.num_tasks == 0) return;
   SpmmArgs a{};
-  for (int s = 0; s < m.S; ++s) {
-    a.ws.col[s] = m.col_ind[s];
-    a.ws.val[s] = m.sp_data[s];
-    a.ws.des[s] = m.group_des[s];
-    a.group_len[s] = s == 0 ? 0 : group_size(s);
-  }
+  a.ws = view_of(m);
   a.tasks = m.tasks;
   a.num_tasks = m.num_tasks;
   a.res_off = m.residue_offset;
@@ -327,13 +324,12 @@ void spmm_launch(const Matrix& m, int N, const float* B, float* C, cudaStream_t 
   a.B = B;
   a.C = C;
   a.ldb = N;
-  const unsigned gx = task_blocks(m.num_tasks);
   if (N % 128 == 0) {
-    spmm_fused<4, 8><<<dim3(gx, N / 128), kThreads, 0, stream>>>(a);
+    spmm_fused<32><<<dim3(task_blocks(m.num_tasks, 32), N / 128), kThreads, 0, stream>>>(a);
   } else if (N % 64 == 0) {
-    spmm_fused<2, 8><<<dim3(gx, N / 64), kThreads, 0, stream>>>(a);
+    spmm_fused<16><<<dim3(task_blocks(m.num_tasks, 16), N / 64), kThreads, 0, stream>>>(a);
   } else {
-    spmm_fused<1, 16><<<dim3(gx, N / 32), kThreads, 0, stream>>>(a);
+    spmm_fused<8><<<dim3(task_blocks(m.num_tasks, 8), N / 32), kThreads, 0, stream>>>(a);
   }
   PSB_LAUNCH_CHECK();
 }
@@ -342,23 +338,18 @@ void sddmm_launch(const Matrix& m, int N, const float* lhs, const float* rhs, fl
                   cudaStream_t stream) {
   if (m.num_tasks == 0) return;
   SddmmArgs a{};
-  for (int s = 0; s < m.S; ++s) {
-    a.ws.col[s] = m.col_ind[s];
-    a.ws.val[s] = m.sp_data[s];
-    a.ws.des[s] = m.group_des[s];
-    a.group_len[s] = s == 0 ? 0 : group_size(s);
-    a.out_ws[s] = out[s];
-  }
+  a.ws = view_of(m);
+  for (int s = 0; s < m.S; ++s) a.out_ws[s] = out[s];
   a.tasks = m.tasks;
   a.num_tasks = m.num_tasks;
   a.res_off = m.residue_offset;
+  a.res_groups = m.group_num[0];
   a.lhs = lhs;
   a.rhs = rhs;
-  const unsigned gx = task_blocks(m.num_tasks);
   if (N == 128) {
-    sddmm_fused<4, 8><<<gx, kThreads, 0, stream>>>(a);
+    sddmm_fused<32><<<task_blocks(m.num_tasks, 32), kThreads, 0, stream>>>(a);
   } else {
-    sddmm_fused<1, 16><<<gx, kThreads, 0, stream>>>(a);
+    sddmm_fused<8><<<task_blocks(m.num_tasks, 8), kThreads, 0, stream>>>(a);
   }
   PSB_LAUNCH_CHECK();
 }
