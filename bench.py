@@ -10,6 +10,9 @@ nnz-balanced row panels, and B (all N x 2.45M rows) is replicated (weak
 scaling; no collective in the timed region).  Inputs are larger than L2
 (B is 1.25 GB per 2.45M rows), so no explicit L2 flush is done.
 
+The JSON line's "extra" object times the other operators of the path (SpMM at
+N=32, SDDMM at N=32 and 128) on the same panel with the same rules.
+
 Prints one JSON line (rank 0).  ``--impl reference`` times the reference's CPU
 path (its FP64 CheckSpmm loop, benchmarks/benchmark.cu:64-77, restated in
 oracle/ps_oracle.cpp) on all host cores on the same workload.
@@ -235,31 +238,50 @@ def main() -> None:
                 "traffic": profile_traffic("spmm_fused", f"cfg2_spmm_n{N}"),
                 "alg_bytes_per_launch": alg_bytes}
 
-    # SpMM at N=32 on the same panel (kernel only, same timing rules).
+    # The other operators of the path on the same panel (kernel only, same timing rules):
+    # SpMM at N=32 and SDDMM at N=32/128 (the reference's N choices).
     extra = {}
-    if N != 32:
-        B32 = B[:, :32].contiguous()
-        C32 = torch.zeros((panel.rows, 32), dtype=torch.float32, device=device)
+
+    def timed(fn, k):
         for _ in range(3):
-            psb.SpMM(m, 32, B32, C32, stream)
+            fn()
         if dist:
             dist.barrier()
         torch.cuda.synchronize(device)
         ev0.record(stream)
-        k32 = max(10, args.steps)
-        for _ in range(k32):
-            psb.SpMM(m, 32, B32, C32, stream)
+        for _ in range(k):
+            fn()
         ev1.record(stream)
         torch.cuda.synchronize(device)
-        ms32 = ev0.elapsed_time(ev1) / k32
+        t = ev0.elapsed_time(ev1) / k
         if dist:
-            t = torch.tensor([ms32], dtype=torch.float64, device=device)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms32 = float(t.item())
+            tt = torch.tensor([t], dtype=torch.float64, device=device)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            t = float(tt.item())
+        return t
+
+    k_extra = max(10, min(args.steps, 50))
+    if N != 32:
+        B32 = B[:, :32].contiguous()
+        C32 = torch.zeros((panel.rows, 32), dtype=torch.float32, device=device)
+        ms32 = timed(lambda: psb.SpMM(m, 32, B32, C32, stream), k_extra)
         ab32 = 8.0 * panel.nnz + 4.0 * 32 * (panel.rows + panel.cols)
         extra["spmm_n32"] = {"ms": round(ms32, 4), "gflops": round(2.0 * nnz_total * 32 / (ms32 * 1e-3) / 1e9, 1),
                              "roofline_frac": round(ab32 / (ms32 * 1e-3) / 1e9 / peak, 4)}
         del B32, C32
+    outs = [torch.zeros(max(m.workset_size(s), 1), dtype=torch.float32, device=device)
+            for s in range(m.GroupTypeNum())]
+    for n_sd in (32, 128):
+        X = B[: panel.rows, :n_sd].contiguous() if panel.rows <= panel.cols else torch.rand(
+            (panel.rows, n_sd), device=device)
+        Y = B[:, :n_sd].contiguous()
+        ms_sd = timed(lambda: psb.SDDMM(m, n_sd, X, Y, outs, stream), k_extra)
+        ab = 12.0 * panel.nnz + 4.0 * n_sd * (panel.rows + panel.cols)
+        extra[f"sddmm_n{n_sd}"] = {"ms": round(ms_sd, 4),
+                                   "gflops": round(2.0 * nnz_total * n_sd / (ms_sd * 1e-3) / 1e9, 1),
+                                   "roofline_frac": round(ab / (ms_sd * 1e-3) / 1e9 / peak, 4)}
+        del X, Y
+    del outs
 
     # End to end through the public API with host buffers: per step, copy B from pinned
     # host memory, zero C, run SpMM, copy C back.
