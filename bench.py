@@ -119,12 +119,16 @@ class ClockSampler:
                 "samples": len(mhz)}
 
 
-def build_workload(rank: int, world: int, device):
+def build_workload(rank: int, world: int, device, workload: str = "cfg2"):
     import powersparse_b200 as psb
     from powersparse_b200 import synth_gpu
-    n_nodes, pairs = synth_gpu.config2_pairs(nodes_scale=world, device=device)
+    if workload == "cfg5":
+        n_nodes, pairs = synth_gpu.config5_pairs(device=device)   # one graph for every N (strong scaling)
+    else:
+        n_nodes, pairs = synth_gpu.config2_pairs(nodes_scale=world, device=device)
     cuts = psb.partition_rows(synth_gpu.global_row_ptr(pairs, n_nodes).astype(np.int32), world)
-    panel = synth_gpu.panel_from_pairs(pairs, n_nodes, int(cuts[rank]), int(cuts[rank + 1]), seed=2)
+    panel = synth_gpu.panel_from_pairs(pairs, n_nodes, int(cuts[rank]), int(cuts[rank + 1]),
+                                       seed=5 if workload == "cfg5" else 2)
     del pairs
     return panel, cuts
 
@@ -160,6 +164,11 @@ def main() -> None:
     ap.add_argument("--n", type=int, default=128)
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["cfg2", "cfg5"], default="cfg2",
+                    help="cfg2: config 2 per GPU (weak scaling, default); cfg5: the config-5 R-MAT graph "
+                         "(16.8M nodes, ~1B nnz) split over the GPUs (strong scaling)")
+    ap.add_argument("--gather", action="store_true",
+                    help="also time the all-gather of the C panels (NCCL) that a replicated result needs")
     args = ap.parse_args()
 
     import torch
@@ -183,7 +192,7 @@ def main() -> None:
         return
 
     import powersparse_b200 as psb
-    panel, cuts = build_workload(rank, world, device)
+    panel, cuts = build_workload(rank, world, device, args.workload)
     m = psb.PowerSparseMatrixGPU(panel.rows, panel.cols, panel.nnz, panel.row_ptr, panel.col_ind, panel.values)
     if rank == 0:
         B = dense_B(panel.cols, N, device)
@@ -232,10 +241,10 @@ def main() -> None:
     alg_bytes = 8.0 * panel.nnz + 4.0 * N * (panel.rows + panel.cols)
     peak, peak_kind = measured_peaks()
     achieved = alg_bytes / (ms_local * 1e-3) / 1e9
-    workload = f"cfg2_spmm_n{N}_x{world}"
+    scaling = "strong" if args.workload == "cfg5" else "weak"
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "peak_source": peak_kind,
-                "traffic": profile_traffic("spmm_fused", f"cfg2_spmm_n{N}"),
+                "traffic": profile_traffic("spmm_fused", f"{args.workload}_spmm_n{N}") if world == 1 else None,
                 "alg_bytes_per_launch": alg_bytes}
 
     # The other operators of the path on the same panel (kernel only, same timing rules):
@@ -283,6 +292,14 @@ def main() -> None:
         del X, Y
     del outs
 
+    if args.gather:
+        # Replicated result: all-gather the C panels over NCCL (outside the timed steps).
+        from powersparse_b200.distributed import allgather_rows
+        full = allgather_rows(C, cuts)
+        tg = timed(lambda: allgather_rows(C, cuts), 5)
+        extra["allgather_c"] = {"ms": round(tg, 3), "bytes_per_gpu_in": int(full.numel() * 4 - C.numel() * 4)}
+        del full
+
     # End to end through the public API with host buffers: per step, copy B from pinned
     # host memory, zero C, run SpMM, copy C back.
     hB = B.cpu().pin_memory()
@@ -328,10 +345,12 @@ def main() -> None:
         line = {
             "metric": METRIC, "value": round(gflops, 1), "unit": "GFLOP/s", "n_gpus": world,
             "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": round(ms, 4),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "f32",
             "data": "synthetic",
-            "config": {"workload": f"cfg2: SpMM N={N}, symmetric Chung-Lu gamma=2.1, {world}x2.45M nodes, "
-                                   f"nnz-balanced row panel per GPU, B replicated",
+            "config": {"workload": (f"cfg2: SpMM N={N}, symmetric Chung-Lu gamma=2.1, {world}x2.45M nodes, "
+                                    f"nnz-balanced row panel per GPU, B replicated") if args.workload == "cfg2" else
+                                   (f"cfg5: SpMM N={N}, R-MAT scale 24 edge factor 64 symmetrised, split into {world} "
+                                    f"nnz-balanced row panels, B replicated"),
                        "rows_per_gpu": panel.rows, "cols": panel.cols, "nnz_per_gpu_rank0": panel.nnz,
                        "nnz_total": nnz_total, "N": N, "S": m.GroupTypeNum(),
                        "parallelism": f"row-panel x{world}", "l2": "inputs larger than L2 (B >= 1.25 GB), no flush",
@@ -349,7 +368,7 @@ def main() -> None:
 def run_reference_arm(args, world: int, device) -> None:
     """The reference's CPU path (FP64 CheckSpmm, restated: no separately callable CPU
     SpMM exists in the reference) on all host cores, on rank 0's panel of the same workload."""
-    panel, _ = build_workload(0, world, device)
+    panel, _ = build_workload(0, world, device, args.workload)
     N = args.n
     B = dense_B(panel.cols, N, device).cpu().numpy()
     from oracle import oracle
@@ -367,8 +386,9 @@ def run_reference_arm(args, world: int, device) -> None:
     v = 2.0 * panel.nnz * N / (ms * 1e-3) / 1e9
     line = {"metric": METRIC, "value": round(v, 2), "unit": "GFLOP/s", "n_gpus": world, "steps": len(times),
             "warmup": min(args.warmup, 1), "ms_per_step": round(ms, 2), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic", "impl": "reference",
-            "config": {"workload": f"cfg2: SpMM N={N}, rank-0 row panel of {world}x2.45M-node graph",
+            "scaling": "strong" if args.workload == "cfg5" else "weak", "vs_baseline": None, "dtype": "f64",
+            "data": "synthetic", "impl": "reference",
+            "config": {"workload": f"{args.workload}: SpMM N={N}, rank-0 row panel ({world} panels)",
                        "rows": panel.rows, "nnz": panel.nnz, "N": N},
             "cpu_baseline": {"value": round(v, 2), "unit": "GFLOP/s", "cores": threads, "kind": "port",
                              "sample": f"one row panel ({panel.nnz} nnz) per step, FP64 CheckSpmm restatement"},

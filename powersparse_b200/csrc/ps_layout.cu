@@ -37,6 +37,7 @@ Matrix::~Matrix() {
   cudaFree(residue_offset);
   cudaFree(residue_atomic);
   cudaFree(tasks);
+  cudaFree(residue_row);
 }
 
 namespace {
@@ -235,6 +236,16 @@ __global__ void gather_group_elements(const uint32_t* __restrict__ order, int G,
       keys[dst + k] = (uint64_t(i) << wcol) | uint64_t(uint32_t(col_ind[p]));
       vals[dst + k] = p;
     }
+  }
+}
+
+__global__ void residue_rows(const int* __restrict__ res_off, const int* __restrict__ des, int groups,
+                             int* __restrict__ row_of) {
+  const int lane = threadIdx.x & 31;
+  const int warps = (gridDim.x * blockDim.x) >> 5;
+  for (int g = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; g < groups; g += warps) {
+    const int r = des[g];
+    for (int e = res_off[g] + lane; e < res_off[g + 1]; e += 32) row_of[e] = r;
   }
 }
 
@@ -532,6 +543,12 @@ Matrix* build_matrix(int rows, int cols, int nnz, const int* row_ptr, const int*
     m->sp_data[s] = val_out.release_ownership();
   }
   m->residue_offset = res_off.release_ownership();
+  if (m->ws_size[0] > 0) {
+    DeviceArray<int> rows_of(size_t(m->ws_size[0]));
+    residue_rows<<<grid_for(G0, 8, kBlocks), 256, 0, st>>>(m->residue_offset, m->group_des[0], G0, rows_of.get());
+    PSB_LAUNCH_CHECK();
+    m->residue_row = rows_of.release_ownership();
+  }
 
   // --- Tasks for the fused kernels.
   const std::vector<Task> tasks = build_tasks(*m, h_res_off);

@@ -46,6 +46,9 @@ struct Matrix {
   // reference layout; derived from it).
   Task* tasks = nullptr;               // device: block tasks (largest groups first), then residue
   int num_tasks = 0;
+  // Destination row of every residue element (residue groups are short, so SDDMM
+  // reads the lhs row per element instead of switching rows at group boundaries).
+  int* residue_row = nullptr;          // device [ws_size[0]]
 
   Matrix() = default;
   Matrix(const Matrix&) = delete;

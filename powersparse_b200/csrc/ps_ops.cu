@@ -189,21 +189,20 @@ struct SddmmArgs {
   WorksetView ws;
   const Task* tasks;
   int num_tasks;
-  const int* res_off;
-  int res_groups;
+  const int* res_row;   // destination row of every residue element
   const float* lhs;
   const float* rhs;
   float* out_ws[kMaxWorksets];
 };
 
-// Reduces kUnroll (= 4) per-lane partial dot products over the LG lanes of a lane
-// group.  Two halving steps on the top two lane bits leave lane l with element
-// (l / (LG / 4)) summed over 4 lanes; butterfly steps on the lower bits finish
-// the sum.
-template <int LG>
-__device__ __forceinline__ float reduce4(float (&p)[4], int l, unsigned gm) {
+// Reduces BATCH per-lane partial dot products over the LG lanes of a lane group:
+// halving steps on the top log2(BATCH) lane bits (each keeps the half of the
+// elements selected by one lane bit and adds the partner's copy of it) leave lane
+// l with element l / (LG / BATCH); butterflies on the lower bits finish the sum.
+template <int LG, int BATCH>
+__device__ __forceinline__ float reduce_batch(float (&p)[BATCH], int l, unsigned gm) {
 #pragma unroll
-  for (int h = 2, bit = LG / 2; h >= 1; h >>= 1, bit >>= 1) {
+  for (int h = BATCH / 2, bit = LG / 2; h >= 1; h >>= 1, bit >>= 1) {
     const bool upper = l & bit;
 #pragma unroll
     for (int i = 0; i < h; ++i) {
@@ -214,22 +213,35 @@ __device__ __forceinline__ float reduce4(float (&p)[4], int l, unsigned gm) {
   }
   float v = p[0];
 #pragma unroll
-  for (int bit = LG / 8; bit >= 1; bit >>= 1) v += __shfl_xor_sync(gm, v, bit, LG);
+  for (int bit = LG / (2 * BATCH); bit >= 1; bit >>= 1) v += __shfl_xor_sync(gm, v, bit, LG);
   return v;
 }
 
-// SDDMM, one task per lane group, N = 4 * LG:
-//   out[e] (+)= val[e] * <lhs[row(g)], rhs[col[e]]>.
+// SDDMM, one task per lane group:  out[e] (+)= val[e] * <lhs[row(e)], rhs[col[e]]>.
+// A lane covers FC chunks of 4 features, chunk c of lane l being features
+// [c*4*LG + 4*l, +4), so every chunk of a dense row is one coalesced 16*LG-byte
+// segment and N = 4 * LG * FC.  Elements are reduced BATCH at a time.
 // Block outputs are stored (sddmm_kernel_block.cu:160-164 of the reference);
-// residue outputs are added, as its residue kernels atomically add into a
-// zeroed buffer (sddmm_kernel_residue.cu:297-305).
-template <int LG>
+// residue outputs are added, as its residue kernels atomically add into a zeroed
+// buffer (sddmm_kernel_residue.cu:297-305).  Residue groups are short, so the
+// residue path loads each element's lhs row alongside its rhs row (per-element
+// rows from the matrix); block groups span whole 32-element chunks, so the block
+// path switches lhs rows once per chunk with the next group's row prefetched.
+template <int LG, int FC, int BATCH>
 __global__ void __launch_bounds__(kThreads) sddmm_fused(const SddmmArgs a) {
-  static_assert(kUnroll == 4, "reduce4 reduces four elements");
+  static_assert(BATCH <= LG && kChunk % BATCH == 0, "batch must fit the lane group and the chunk");
+  constexpr int kLoadGroup = BATCH < kUnroll ? BATCH : kUnroll;  // gathers issued together
+  // Reusing a residue element's lhs row for the next element of the same group
+  // pays at N = 128 (512-byte rows) and costs more than it saves at N = 32.
+  constexpr bool kReuseRows = 4 * LG * FC >= 128;
+  static_assert(BATCH % kLoadGroup == 0, "load groups tile the batch");
   constexpr int NG = 32 / LG;
-  constexpr int kLanesPerElem = LG / 4;
+  constexpr int kLanesPerElem = LG / BATCH;
+  constexpr int SEG = 4 * LG;
+  constexpr long long N = (long long)SEG * FC;
   __shared__ int s_col[kWarpsPerBlock][NG][kChunk + 1];
   __shared__ float s_val[kWarpsPerBlock][NG][kChunk + 1];
+  __shared__ int s_row[kWarpsPerBlock][NG][kChunk + 1];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q = lane / LG, l = lane % LG;
   const unsigned gm = LG == 32 ? 0xffffffffu : (((1u << LG) - 1u) << (q * LG));
@@ -238,56 +250,122 @@ __global__ void __launch_bounds__(kThreads) sddmm_fused(const SddmmArgs a) {
   const Task t = a.tasks[task_id];
   const int* __restrict__ col = a.ws.col[t.ws];
   const float* __restrict__ val = a.ws.val[t.ws];
-  const int* __restrict__ des = a.ws.des[t.ws];
   float* __restrict__ out = a.out_ws[t.ws];
-  const long long N = 4 * LG;
   const float* __restrict__ rhs_l = a.rhs + 4 * l;
   const float* __restrict__ lhs_l = a.lhs + 4 * l;
   int* sc = s_col[warp][q];
   float* sv = s_val[warp][q];
-  const bool residue = t.ws == 0;
-  const int G = a.ws.group_len[t.ws];
-  auto lhs_row = [&](int gi) { return __ldg(reinterpret_cast<const float4*>(lhs_l + (long long)des[gi] * N)); };
+  int* sr = s_row[warp][q];
+  auto seg = [](const float* base, long long row, int c) {
+    return __ldg(reinterpret_cast<const float4*>(base + row * N + c * SEG));
+  };
 
+  if (t.ws == 0) {
+    float4 xc[FC];  // lhs row segments of the last element handled
+    for (int base = t.begin; base < t.end; base += kChunk) {
+      const int n = min(kChunk, t.end - base);
+      const int last_row = base == t.begin ? -1 : sr[kChunk - 1];
+      __syncwarp(gm);
+#pragma unroll
+      for (int r = 0; r < kChunk / LG; ++r) {
+        const int i = l + r * LG;
+        if (i < n) {
+          sc[i] = __ldcs(col + base + i);
+          sv[i] = __ldcs(val + base + i);
+          sr[i] = __ldcs(a.res_row + base + i);
+        }
+      }
+      if (l == 0) sr[kChunk] = last_row;
+      __syncwarp(gm);
+      for (int j = 0; j < n; j += BATCH) {
+        float p[BATCH];
+#pragma unroll
+        for (int u = 0; u < BATCH; ++u) p[u] = 0.f;
+#pragma unroll
+        for (int c = 0; c < FC; ++c) {
+#pragma unroll
+          for (int h = 0; h < BATCH; h += kLoadGroup) {
+            // Consecutive elements of a group share their lhs row: with kReuseRows,
+            // load it only where the row changes (issued with the rhs loads) and
+            // copy it otherwise.
+            float4 y[kLoadGroup], x[kLoadGroup];
+            bool fresh[kLoadGroup];
+#pragma unroll
+            for (int u = 0; u < kLoadGroup; ++u) {
+              const int e = j + h + u;
+              fresh[u] = !kReuseRows || sr[e] != (e == 0 ? sr[kChunk] : sr[e - 1]);
+              if (e < n) {
+                y[u] = seg(rhs_l, sc[e], c);
+                if (fresh[u]) x[u] = seg(lhs_l, sr[e], c);
+              }
+            }
+#pragma unroll
+            for (int u = 0; u < kLoadGroup; ++u) {
+              if (j + h + u < n) {
+                if (!fresh[u]) x[u] = u == 0 ? xc[c] : x[u - 1];
+                p[h + u] += dot4(x[u], y[u]);
+              }
+            }
+            xc[c] = x[kLoadGroup - 1];
+          }
+        }
+        const float dot = reduce_batch<LG, BATCH>(p, l, gm);
+        const int jl = j + l / kLanesPerElem;
+        if (l % kLanesPerElem == 0 && jl < n) atomicAdd(out + base + jl, dot * sv[jl]);
+      }
+      __syncwarp(gm);
+    }
+    return;
+  }
+
+  const int* __restrict__ des = a.ws.des[t.ws];
+  const int G = a.ws.group_len[t.ws];
+  const int groups = a.ws.groups[t.ws];
   int g = t.group;
-  int cur_end = residue ? a.res_off[g + 1] : (g + 1) * G;
-  float4 x = lhs_row(g);
+  float4 x[FC], x_next[FC];
+#pragma unroll
+  for (int c = 0; c < FC; ++c) x[c] = seg(lhs_l, des[g], c);
+  const bool more = g + 1 < groups && (g + 1) * G < t.end;
+  if (more) {
+#pragma unroll
+    for (int c = 0; c < FC; ++c) x_next[c] = seg(lhs_l, des[g + 1], c);
+  }
   for (int base = t.begin; base < t.end; base += kChunk) {
-    const int n = min(kChunk, t.end - base);
+    if (base != t.begin && base % G == 0) {  // the chunk starts group g + 1
+      ++g;
+#pragma unroll
+      for (int c = 0; c < FC; ++c) x[c] = x_next[c];
+      if (g + 1 < groups && (g + 1) * G < t.end) {
+#pragma unroll
+        for (int c = 0; c < FC; ++c) x_next[c] = seg(lhs_l, des[g + 1], c);
+      }
+    }
 #pragma unroll
     for (int r = 0; r < kChunk / LG; ++r) {
       const int i = l + r * LG;
-      if (i < n) {
-        sc[i] = __ldcs(col + base + i);
-        sv[i] = __ldcs(val + base + i);
-      }
+      sc[i] = __ldcs(col + base + i);
+      sv[i] = __ldcs(val + base + i);
     }
     __syncwarp(gm);
-    for (int j = 0; j < n; j += kUnroll) {
-      float4 y[kUnroll];
+#pragma unroll 1
+    for (int j = 0; j < kChunk; j += BATCH) {
+      float p[BATCH];
 #pragma unroll
-      for (int u = 0; u < kUnroll; ++u)
-        if (j + u < n) y[u] = __ldg(reinterpret_cast<const float4*>(rhs_l + (long long)sc[j + u] * N));
-      float p[kUnroll];
+      for (int u = 0; u < BATCH; ++u) p[u] = 0.f;
 #pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        p[u] = 0.f;
-        if (j + u < n) {
-          if (base + j + u == cur_end) {
-            ++g;
-            cur_end = residue ? a.res_off[g + 1] : (g + 1) * G;
-            x = lhs_row(g);
-          }
-          p[u] = dot4(x, y[u]);
+      for (int c = 0; c < FC; ++c) {
+#pragma unroll
+        for (int h = 0; h < BATCH; h += kLoadGroup) {
+          float4 y[kLoadGroup];
+#pragma unroll
+          for (int u = 0; u < kLoadGroup; ++u) y[u] = seg(rhs_l, sc[j + h + u], c);
+#pragma unroll
+          for (int u = 0; u < kLoadGroup; ++u) p[h + u] += dot4(x[c], y[u]);
         }
       }
-      const float dot = reduce4<LG>(p, l, gm);
+      const float dot = reduce_batch<LG, BATCH>(p, l, gm);
       const int jl = j + l / kLanesPerElem;
-      if (l % kLanesPerElem == 0 && jl < n) {
-        const float r = dot * sv[jl];
-        if (residue) atomicAdd(out + base + jl, r);
-        else out[base + jl] = r;
-      }
+      if (l % kLanesPerElem == 0) out[base + jl] = dot * sv[jl];
     }
     __syncwarp(gm);
   }
@@ -342,14 +420,13 @@ void sddmm_launch(const Matrix& m, int N, const float* lhs, const float* rhs, fl
   for (int s = 0; s < m.S; ++s) a.out_ws[s] = out[s];
   a.tasks = m.tasks;
   a.num_tasks = m.num_tasks;
-  a.res_off = m.residue_offset;
-  a.res_groups = m.group_num[0];
+  a.res_row = m.residue_row;
   a.lhs = lhs;
   a.rhs = rhs;
   if (N == 128) {
-    sddmm_fused<32><<<task_blocks(m.num_tasks, 32), kThreads, 0, stream>>>(a);
+    sddmm_fused<16, 2, 4><<<task_blocks(m.num_tasks, 16), kThreads, 0, stream>>>(a);
   } else {
-    sddmm_fused<8><<<task_blocks(m.num_tasks, 8), kThreads, 0, stream>>>(a);
+    sddmm_fused<8, 1, 8><<<task_blocks(m.num_tasks, 8), kThreads, 0, stream>>>(a);
   }
   PSB_LAUNCH_CHECK();
 }

@@ -106,8 +106,43 @@ def global_row_ptr(pairs: torch.Tensor, n: int) -> np.ndarray:
     return rp.cpu().numpy()
 
 
-# Config 2's degree law (see synth.CONFIGS[2]); ``nodes_scale`` multiplies the node count.
+def rmat_pairs(scale: int, edge_factor: int, seed: int, abcd=(0.57, 0.19, 0.19, 0.05), device="cuda",
+               chunk: int = 1 << 25) -> tuple[int, torch.Tensor]:
+    """Unique undirected pairs of an R-MAT graph (2^scale nodes, edge_factor * 2^scale / 2
+    sampled pairs, self loops dropped, node labels randomly permuted), as sorted keys."""
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed)
+    n = 1 << scale
+    m = edge_factor * n // 2
+    a, b, c, _ = abcd
+    perm = torch.randperm(n, generator=gen, device=device)
+    keys = []
+    for s0 in range(0, m, chunk):
+        k = min(chunk, m - s0)
+        u = torch.zeros(k, dtype=torch.int64, device=device)
+        v = torch.zeros(k, dtype=torch.int64, device=device)
+        for bit in range(scale):
+            x = torch.rand(k, generator=gen, device=device)
+            down = x >= a + b
+            right = ((x >= a) & (x < a + b)) | (x >= a + b + c)
+            u |= down.to(torch.int64) << bit
+            v |= right.to(torch.int64) << bit
+        u = perm[u]
+        v = perm[v]
+        keep = u != v
+        u, v = u[keep], v[keep]
+        keys.append(torch.unique(torch.minimum(u, v) * n + torch.maximum(u, v)))
+    return n, torch.unique(torch.cat(keys))
+
+
+def config5_pairs(device="cuda"):
+    """Configuration 5: R-MAT scale 24, edge factor 64, (a,b,c,d) = (.57,.19,.19,.05)."""
+    p = synth.CONFIGS[5]
+    return rmat_pairs(p["scale"], p["edge_factor"], seed=5, device=device)
+
+
 def config2_pairs(nodes_scale: int = 1, device="cuda"):
+    """Config 2's degree law (synth.CONFIGS[2]); ``nodes_scale`` multiplies the node count."""
     p = synth.CONFIGS[2]
     n = p["n"] * nodes_scale
     return n, chung_lu_pairs(n, p["mean"], p["dmax"], p["gamma"], seed=2, oversample=p["oversample"],
