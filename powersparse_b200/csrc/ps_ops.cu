@@ -75,10 +75,11 @@ struct SpmmArgs {
 // spmm_kernel_residue.cu:68-81 of the reference.  Block groups accumulate FP32
 // per 32-element chunk and carry the running sum in FP64.
 template <int LG>
-__global__ void __launch_bounds__(kThreads) spmm_fused(const SpmmArgs a) {
+__global__ void __launch_bounds__(kThreads, 4) spmm_fused(const SpmmArgs a) {
   constexpr int NG = 32 / LG;
-  __shared__ int s_col[kWarpsPerBlock][NG][kChunk + 1];
-  __shared__ float s_val[kWarpsPerBlock][NG][kChunk + 1];
+  // (column, value bits) of the staged chunk; odd stride keeps lane groups on
+  // different banks.
+  __shared__ int2 s_cv[kWarpsPerBlock][NG][kChunk + 1];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q = lane / LG, l = lane % LG;
   const unsigned gm = LG == 32 ? 0xffffffffu : (((1u << LG) - 1u) << (q * LG));
@@ -91,16 +92,12 @@ __global__ void __launch_bounds__(kThreads) spmm_fused(const SpmmArgs a) {
   const int colofs = blockIdx.y * (4 * LG) + l * 4;
   const float* __restrict__ Bl = a.B + colofs;
   float* __restrict__ Cl = a.C + colofs;
-  int* sc = s_col[warp][q];
-  float* sv = s_val[warp][q];
+  int2* cv = s_cv[warp][q];
   auto stage = [&](int base, int n) {
 #pragma unroll
     for (int r = 0; r < kChunk / LG; ++r) {
       const int i = l + r * LG;
-      if (i < n) {
-        sc[i] = __ldcs(col + base + i);
-        sv[i] = __ldcs(val + base + i);
-      }
+      if (i < n) cv[i] = make_int2(__ldcs(col + base + i), __float_as_int(__ldcs(val + base + i)));
     }
   };
   auto gather = [&](int c) { return __ldg(reinterpret_cast<const float4*>(Bl + (long long)c * a.ldb)); };
@@ -125,9 +122,15 @@ __global__ void __launch_bounds__(kThreads) spmm_fused(const SpmmArgs a) {
       __syncwarp(gm);
       for (int j = 0; j < n; j += kUnroll) {
         float4 b[kUnroll];
+        float sv[kUnroll];
 #pragma unroll
-        for (int u = 0; u < kUnroll; ++u)
-          if (j + u < n) b[u] = gather(sc[j + u]);
+        for (int u = 0; u < kUnroll; ++u) {
+          if (j + u < n) {
+            const int2 e = cv[j + u];
+            b[u] = gather(e.x);
+            sv[u] = __int_as_float(e.y);
+          }
+        }
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
           if (j + u < n) {
@@ -147,7 +150,7 @@ __global__ void __launch_bounds__(kThreads) spmm_fused(const SpmmArgs a) {
               cur_row = __shfl_sync(gm, g_row, widx, LG);
               cur_atomic = __shfl_sync(gm, g_atomic, widx, LG);
             }
-            fma4(acc, sv[j + u], b[u]);
+            fma4(acc, sv[u], b[u]);
           }
         }
       }
@@ -168,10 +171,15 @@ __global__ void __launch_bounds__(kThreads) spmm_fused(const SpmmArgs a) {
 #pragma unroll 1
     for (int j = 0; j < kChunk; j += kUnroll) {
       float4 b[kUnroll];
+      float sv[kUnroll];
 #pragma unroll
-      for (int u = 0; u < kUnroll; ++u) b[u] = gather(sc[j + u]);
+      for (int u = 0; u < kUnroll; ++u) {
+        const int2 e = cv[j + u];
+        b[u] = gather(e.x);
+        sv[u] = __int_as_float(e.y);
+      }
 #pragma unroll
-      for (int u = 0; u < kUnroll; ++u) fma4(acc, sv[j + u], b[u]);
+      for (int u = 0; u < kUnroll; ++u) fma4(acc, sv[u], b[u]);
     }
     __syncwarp(gm);
     dx += acc.x; dy += acc.y; dz += acc.z; dw += acc.w;
