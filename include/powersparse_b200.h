@@ -86,6 +86,11 @@ double ps_matrix_preprocess_ms(const ps_matrix* matrix);
 /* CUDA device the matrix lives on. */
 int ps_matrix_device(const ps_matrix* matrix);
 
+/* Rows whose block slices SpMM sums in FP64 before adding them to C (rows cut
+ * into at least 8 block slices of 256 elements).  No reference counterpart: the
+ * reference adds every block group to C in FP32. */
+int ps_matrix_wide_rows(const ps_matrix* matrix);
+
 /* FP32 C (+)= A * B on `stream`, asynchronous.  B is [MatrixCol() x N] and C is
  * [MatrixRow() x N], both row-major device arrays; zero C before each
  * independent call.  N: positive multiple of 32 with N/32 <= 65535.  Replaces

@@ -61,6 +61,7 @@ _SIGNATURES = [
     ("ps_matrix_workset_size", ctypes.c_longlong, [_vp, ctypes.c_int]),
     ("ps_matrix_preprocess_ms", ctypes.c_double, [_vp]),
     ("ps_matrix_device", ctypes.c_int, [_vp]),
+    ("ps_matrix_wide_rows", ctypes.c_int, [_vp]),
     ("ps_spmm", ctypes.c_int, [_vp, ctypes.c_int, _vp, _vp, _vp]),
     ("ps_sddmm", ctypes.c_int, [_vp, ctypes.c_int, _vp, _vp, ctypes.POINTER(_vp), _vp]),
     ("ps_partition_rows", ctypes.c_int, [ctypes.c_int, _i32p, ctypes.c_int, _i32p]),
@@ -218,6 +219,11 @@ class PowerSparseMatrixGPU:
     @property
     def device(self) -> int:
         return int(load_library().ps_matrix_device(self.handle))
+
+    @property
+    def wide_rows(self) -> int:
+        """Rows whose block slices SpMM sums in FP64 (ps_matrix_wide_rows)."""
+        return int(load_library().ps_matrix_wide_rows(self.handle))
 
     def download(self) -> dict:
         """Copy the layout to host numpy arrays (ReadWorkset of benchmarks/benchmark.cu:29-41)."""

@@ -97,6 +97,7 @@ long long ps_matrix_workset_size(const ps_matrix* h, int s) {
 }
 double ps_matrix_preprocess_ms(const ps_matrix* h) { return M(h).preprocess_ms; }
 int ps_matrix_device(const ps_matrix* h) { return M(h).device; }
+int ps_matrix_wide_rows(const ps_matrix* h) { return M(h).wide_rows; }
 
 int ps_spmm(const ps_matrix* h, int N, const float* B, float* C, void* stream) {
   return guarded([&] {

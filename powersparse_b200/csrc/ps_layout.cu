@@ -27,6 +27,7 @@
 #include <memory>
 #include <numeric>
 #include <stdexcept>
+#include <unordered_map>
 
 namespace psb {
 
@@ -36,8 +37,11 @@ Matrix::~Matrix() {
   for (auto p : group_des) cudaFree(p);
   cudaFree(residue_offset);
   cudaFree(residue_atomic);
-  cudaFree(tasks);
+  for (auto p : tasks) cudaFree(p);
   cudaFree(residue_row);
+  cudaFree(wide_row);
+  cudaFree(wide_acc);
+  if (wide_ready) cudaEventDestroy(wide_ready);
 }
 
 namespace {
@@ -319,32 +323,51 @@ void validate_csr(int rows, int cols, int nnz, const int* row_ptr, const int* co
 }
 
 // Splits every workset into tasks of about kTaskElems elements, largest group
-// sizes first (the reference launches worksets S-1 down to 0).
-std::vector<Task> build_tasks(const Matrix& m, const std::vector<int>& h_res_off) {
+// sizes first (the reference launches worksets S-1 down to 0), in one of the
+// two orders of TaskOrder.
+//
+// Why two orders (measured on B200, configurations 2-4): a row's most frequent
+// columns sit in its largest groups and each group's columns are ascending, so
+// slice k of the groups of one workset gathers from largely the same hot rows of
+// the dense operand.  Running those slices side by side (kSliceOrder) turns that
+// into L1/L2 hits when a dense row spans several cache lines (N >= 128: -4% to
+// -10% time).  With one-line rows (N = 32) the same order concentrates the
+// requests of every SM on a few lines at once and is slower, and there the
+// residue, which runs last, is cut finer so that the tail of the launch drains
+// quickly.
+// `slot_of[s][g]`: wide-row slot of block group g of workset s (empty: none).
+std::vector<Task> build_tasks(const Matrix& m, const std::vector<int>& h_res_off, TaskOrder order,
+                              const std::vector<std::vector<int>>& slot_of) {
+  auto slot = [&](int s, int g) { return slot_of[s].empty() ? -1 : slot_of[s][g]; };
   std::vector<Task> tasks;
   for (int s = m.S - 1; s >= 1; --s) {
     const int G = group_size(s);
     const int groups = m.group_num[s];
-    if (G >= kTaskElems) {
+    if (G >= kTaskElems && order == kRowOrder) {
       for (int g = 0; g < groups; ++g)
         for (int off = 0; off < G; off += kTaskElems)
-          tasks.push_back({s, g * G + off, g * G + std::min(G, off + kTaskElems), g});
+          tasks.push_back({s, g * G + off, g * G + std::min(G, off + kTaskElems), g, slot(s, g)});
+    } else if (G >= kTaskElems) {
+      for (int off = 0; off < G; off += kTaskElems)
+        for (int g = 0; g < groups; ++g)
+          tasks.push_back({s, g * G + off, g * G + std::min(G, off + kTaskElems), g, slot(s, g)});
     } else {
       const int per = kTaskElems / G;
       for (int g = 0; g < groups; g += per) {
         const int ge = std::min(groups, g + per);
-        tasks.push_back({s, g * G, ge * G, g});
+        tasks.push_back({s, g * G, ge * G, g, -1});
       }
     }
   }
   const int G0 = m.group_num[0];
+  const int residue_elems = order == kRowOrder ? kNarrowResidueTaskElems : kTaskElems;
   int g = 0;
   while (g < G0) {
     const int first = g;
     const int begin = h_res_off[g];
-    while (g < G0 && h_res_off[g + 1] - begin <= kTaskElems) ++g;
+    while (g < G0 && h_res_off[g + 1] - begin <= residue_elems) ++g;
     if (g == first) ++g;  // a single group longer than a task (cannot happen: <= 31 or 16)
-    tasks.push_back({0, begin, h_res_off[g], first});
+    tasks.push_back({0, begin, h_res_off[g], first, -1});
   }
   return tasks;
 }
@@ -551,11 +574,51 @@ Matrix* build_matrix(int rows, int cols, int nnz, const int* row_ptr, const int*
   }
 
   // --- Tasks for the fused kernels.
-  const std::vector<Task> tasks = build_tasks(*m, h_res_off);
-  m->num_tasks = int(tasks.size());
-  if (!tasks.empty()) {
-    PSB_CUDA(cudaMalloc(reinterpret_cast<void**>(&m->tasks), sizeof(Task) * tasks.size()));
-    PSB_CUDA(cudaMemcpy(m->tasks, tasks.data(), sizeof(Task) * tasks.size(), cudaMemcpyHostToDevice));
+  // Wide rows (kWideRowSlices): block slices per row from its length, the same
+  // split into worksets as group_metadata makes; slots in row order.
+  std::vector<std::vector<int>> slot_of(S);
+  {
+    std::unordered_map<int, int> slot_of_row;
+    std::vector<int> h_wide_row;
+    for (int r = 0; r < rows && S > 1; ++r) {
+      int rest = row_ptr[r + 1] - row_ptr[r];
+      if (rest < kWideRowSlices * kTaskElems) continue;
+      long long slices = 0;
+      for (int s = S - 1; s >= 1; --s) {
+        const int G = group_size(s);
+        const int g = rest / G;
+        if (G >= kTaskElems) slices += (long long)g * (G / kTaskElems);
+        rest -= g * G;
+      }
+      if (slices >= kWideRowSlices) {
+        slot_of_row.emplace(r, int(h_wide_row.size()));
+        h_wide_row.push_back(r);
+      }
+    }
+    m->wide_rows = int(h_wide_row.size());
+    if (m->wide_rows > 0) {
+      for (int s = 1; s < S; ++s) {
+        if (group_size(s) < kTaskElems || m->group_num[s] == 0) continue;
+        std::vector<int> h_des(m->group_num[s]);
+        PSB_CUDA(cudaMemcpy(h_des.data(), m->group_des[s], sizeof(int) * h_des.size(), cudaMemcpyDeviceToHost));
+        slot_of[s].assign(h_des.size(), -1);
+        for (size_t g = 0; g < h_des.size(); ++g) {
+          const auto it = slot_of_row.find(h_des[g]);
+          if (it != slot_of_row.end()) slot_of[s][g] = it->second;
+        }
+      }
+      PSB_CUDA(cudaMalloc(reinterpret_cast<void**>(&m->wide_row), sizeof(int) * h_wide_row.size()));
+      PSB_CUDA(cudaMemcpy(m->wide_row, h_wide_row.data(), sizeof(int) * h_wide_row.size(), cudaMemcpyHostToDevice));
+      PSB_CUDA(cudaEventCreateWithFlags(&m->wide_ready, cudaEventDisableTiming));
+    }
+  }
+  for (int o = 0; o < kNumTaskOrders; ++o) {
+    const std::vector<Task> tasks = build_tasks(*m, h_res_off, TaskOrder(o), slot_of);
+    m->num_tasks[o] = int(tasks.size());
+    if (!tasks.empty()) {
+      PSB_CUDA(cudaMalloc(reinterpret_cast<void**>(&m->tasks[o]), sizeof(Task) * tasks.size()));
+      PSB_CUDA(cudaMemcpy(m->tasks[o], tasks.data(), sizeof(Task) * tasks.size(), cudaMemcpyHostToDevice));
+    }
   }
   PSB_CUDA(cudaDeviceSynchronize());
   m->preprocess_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();

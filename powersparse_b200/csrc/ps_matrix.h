@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <mutex>
 #include <vector>
 
 namespace psb {
@@ -17,12 +18,22 @@ inline int group_size(int s) { return 32 << (s - 1); }
 // A unit of SpMM/SDDMM work: elements [begin, end) of workset `ws`, starting in
 // group `group`.  Residue tasks cover whole groups; block tasks cover whole
 // groups, or one slice of a group when the group is longer than a task.
+// `slot` >= 0 marks a slice of a wide row (see Matrix::wide_rows).
 struct Task {
   int ws;
   int begin;
   int end;
   int group;
+  int slot;
 };
+
+// The same tasks in two orders (build_matrix makes both; the operators pick one
+// by the width of a dense row):
+//   kRowOrder    slices of one group consecutive, residue tasks of at most
+//                kNarrowResidueTaskElems elements.  For rows of < 512 bytes.
+//   kSliceOrder  per workset, slice k of every group before slice k+1, residue
+//                tasks of at most kTaskElems elements.  For rows of >= 512 bytes.
+enum TaskOrder { kRowOrder = 0, kSliceOrder = 1, kNumTaskOrders = 2 };
 
 struct Matrix {
   int device = 0;
@@ -44,11 +55,24 @@ struct Matrix {
 
   // Work decomposition for the fused SpMM / SDDMM kernels (not part of the
   // reference layout; derived from it).
-  Task* tasks = nullptr;               // device: block tasks (largest groups first), then residue
-  int num_tasks = 0;
+  // Per order: device tasks, block worksets (largest groups first), then the residue.
+  Task* tasks[kNumTaskOrders] = {};
+  int num_tasks[kNumTaskOrders] = {};
   // Destination row of every residue element (residue groups are short, so SDDMM
   // reads the lhs row per element instead of switching rows at group boundaries).
   int* residue_row = nullptr;          // device [ws_size[0]]
+
+  // Wide rows: rows split into at least kWideRowSlices block-slice tasks.  SpMM
+  // sums their slices in FP64 (one slot of N doubles per row) and folds the sum
+  // into C once, instead of adding every slice to C in FP32.
+  int wide_rows = 0;
+  int* wide_row = nullptr;             // device [wide_rows]: row of each slot
+  // FP64 scratch of the wide rows, grown on demand to wide_rows * N doubles and
+  // all-zero between calls.  Calls that use it are ordered by `wide_ready`.
+  mutable double* wide_acc = nullptr;
+  mutable long long wide_acc_cap = 0;  // doubles
+  mutable cudaEvent_t wide_ready = nullptr;
+  mutable std::mutex wide_mutex;
 
   Matrix() = default;
   Matrix(const Matrix&) = delete;
@@ -63,7 +87,14 @@ struct Matrix {
 Matrix* build_matrix(int rows, int cols, int nnz, const int* row_ptr, const int* col_ind,
                      const float* sp_data, int sm_count);
 
-// Task size in elements used by build_matrix.
+// Task sizes in elements used by build_matrix.
 constexpr int kTaskElems = 256;
+constexpr int kNarrowResidueTaskElems = 64;
+// Rows with at least this many block slices are wide rows (FP64 slice sums).
+// A slice partial is rounded once per FP32 add into C; with k adds of a running
+// sum of magnitude R the rounding drift is about sqrt(k) * 2^-24 * R, which for
+// k >= 8 (rows of >= 2048 elements, R ~ sqrt(row length)) reaches 1e-5, the
+// absolute tolerance, on outputs whose exact value is near zero.
+constexpr int kWideRowSlices = 8;
 
 }  // namespace psb

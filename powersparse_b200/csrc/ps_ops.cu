@@ -3,7 +3,7 @@
 // The reference launches one kernel per workset on its own stream and
 // device-synchronizes (PowerSparse_SpMM/spmm_solution.cu:16-33,
 // PowerSparse_SDDMM/sddmm_solution.cu:23-49).  Here one launch covers every
-// workset: the matrix carries a task list (ps_matrix.h: about kTaskElems
+// workset: the matrix carries task lists (ps_matrix.h: about kTaskElems
 // elements per task, largest groups first) and each lane group runs one task.
 //
 // Lane groups: LG lanes (8, 16 or 32) handle one sparse element at a time, each
@@ -22,6 +22,9 @@
 #include "ps_common.cuh"
 #include "ps_matrix.h"
 #include "ps_ops.h"
+
+#include <algorithm>
+#include <stdexcept>
 
 namespace psb {
 namespace {
@@ -66,6 +69,7 @@ struct SpmmArgs {
   const float* B;
   float* C;
   long long ldb;  // N
+  double* wide_acc;  // [wide rows][N] FP64 slice sums (tasks with slot >= 0)
 };
 
 // SpMM, one task per lane group:
@@ -186,7 +190,17 @@ __global__ void __launch_bounds__(kThreads, 4) spmm_fused(const SpmmArgs a) {
     acc = make_float4(0.f, 0.f, 0.f, 0.f);
     const int next = base + kChunk;
     if (next == t.end || next % G == 0) {
-      emit4(Cl + (long long)des[g] * a.ldb, make_float4(float(dx), float(dy), float(dz), float(dw)), true);
+      if (t.slot >= 0) {
+        // A slice of a wide row (one group per task): FP64 sum, folded into C
+        // by wide_rows_fold after the launch.
+        double* acc = a.wide_acc + (long long)t.slot * a.ldb + colofs;
+        atomicAdd(acc, dx);
+        atomicAdd(acc + 1, dy);
+        atomicAdd(acc + 2, dz);
+        atomicAdd(acc + 3, dw);
+      } else {
+        emit4(Cl + (long long)des[g] * a.ldb, make_float4(float(dx), float(dy), float(dz), float(dw)), true);
+      }
       dx = dy = dz = dw = 0.0;
       ++g;
     }
@@ -379,6 +393,30 @@ __global__ void __launch_bounds__(kThreads) sddmm_fused(const SddmmArgs a) {
   }
 }
 
+// C[wide_row[slot], :] = float(C + acc[slot, :]) (one rounding), then acc = 0
+// so that the scratch is all-zero for the next call.
+__global__ void __launch_bounds__(256) wide_rows_fold(const int* __restrict__ wide_row, int wide_rows, int N,
+                                                      double* __restrict__ acc, float* __restrict__ C) {
+  const int per_row = N / 4;
+  const long long total = (long long)wide_rows * per_row;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long slot = i / per_row;
+    const int q = int(i - slot * per_row);
+    double2* a2 = reinterpret_cast<double2*>(acc + slot * N + 4 * q);
+    float4* c4 = reinterpret_cast<float4*>(C + (long long)wide_row[slot] * N + 4 * q);
+    const double2 lo = a2[0], hi = a2[1];
+    float4 c = *c4;
+    c.x = float(double(c.x) + lo.x);
+    c.y = float(double(c.y) + lo.y);
+    c.z = float(double(c.z) + hi.x);
+    c.w = float(double(c.w) + hi.y);
+    *c4 = c;
+    a2[0] = make_double2(0.0, 0.0);
+    a2[1] = make_double2(0.0, 0.0);
+  }
+}
+
 unsigned task_blocks(int num_tasks, int lane_group) {
   const long long per_block = (long long)kWarpsPerBlock * (32 / lane_group);
   return unsigned((num_tasks + per_block - 1) / per_block);
@@ -396,45 +434,82 @@ WorksetView view_of(const Matrix& m) {
   return v;
 }
 
+// Task order for dense rows of N floats (TaskOrder in ps_matrix.h).
+TaskOrder order_for(int N) { return N >= 128 ? kSliceOrder : kRowOrder; }
+
 }  // namespace
 
 void spmm_launch(const Matrix& m, int N, const float* B, float* C, cudaStream_t stream) {
-  if (m.num_tasks == 0) return;
+  const TaskOrder o = order_for(N);
+  if (m.num_tasks[o] == 0) return;
   SpmmArgs a{};
   a.ws = view_of(m);
-  a.tasks = m.tasks;
-  a.num_tasks = m.num_tasks;
+  a.tasks = m.tasks[o];
+  a.num_tasks = m.num_tasks[o];
   a.res_off = m.residue_offset;
   a.res_atomic = m.residue_atomic;
   a.res_groups = m.group_num[0];
   a.B = B;
   a.C = C;
   a.ldb = N;
-  if (N % 128 == 0) {
-    spmm_fused<32><<<dim3(task_blocks(m.num_tasks, 32), N / 128), kThreads, 0, stream>>>(a);
-  } else if (N % 64 == 0) {
-    spmm_fused<16><<<dim3(task_blocks(m.num_tasks, 16), N / 64), kThreads, 0, stream>>>(a);
-  } else {
-    spmm_fused<8><<<dim3(task_blocks(m.num_tasks, 8), N / 32), kThreads, 0, stream>>>(a);
+  auto launch = [&] {
+    if (N % 128 == 0) {
+      spmm_fused<32><<<dim3(task_blocks(a.num_tasks, 32), N / 128), kThreads, 0, stream>>>(a);
+    } else if (N % 64 == 0) {
+      spmm_fused<16><<<dim3(task_blocks(a.num_tasks, 16), N / 64), kThreads, 0, stream>>>(a);
+    } else {
+      spmm_fused<8><<<dim3(task_blocks(a.num_tasks, 8), N / 32), kThreads, 0, stream>>>(a);
+    }
+    PSB_LAUNCH_CHECK();
+  };
+  if (m.wide_rows == 0) {
+    launch();
+    return;
   }
+  // Wide rows: the matrix's FP64 scratch.  Calls that share it are serialized on
+  // the device through wide_ready (the scratch is all-zero again when a call's
+  // fold kernel ends); a larger N grows it once, after the last user finished.
+  std::lock_guard<std::mutex> lock(m.wide_mutex);
+  const long long need = (long long)m.wide_rows * N;
+  cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+  PSB_CUDA(cudaStreamIsCapturing(stream, &capture));
+  if (m.wide_acc_cap < need) {
+    if (capture != cudaStreamCaptureStatusNone)
+      throw std::runtime_error("SpMM at a new N cannot be captured: call it once with this N before capturing");
+    PSB_CUDA(cudaEventSynchronize(m.wide_ready));
+    PSB_CUDA(cudaFree(m.wide_acc));
+    m.wide_acc = nullptr;
+    m.wide_acc_cap = 0;
+    PSB_CUDA(cudaMalloc(reinterpret_cast<void**>(&m.wide_acc), sizeof(double) * size_t(need)));
+    PSB_CUDA(cudaMemset(m.wide_acc, 0, sizeof(double) * size_t(need)));
+    m.wide_acc_cap = need;
+  }
+  if (capture == cudaStreamCaptureStatusNone) PSB_CUDA(cudaStreamWaitEvent(stream, m.wide_ready, 0));
+  a.wide_acc = m.wide_acc;
+  launch();
+  const long long total = (long long)m.wide_rows * (N / 4);
+  const unsigned blocks = unsigned(std::min<long long>((total + 255) / 256, 148LL * 8));
+  wide_rows_fold<<<blocks, 256, 0, stream>>>(m.wide_row, m.wide_rows, N, m.wide_acc, C);
   PSB_LAUNCH_CHECK();
+  if (capture == cudaStreamCaptureStatusNone) PSB_CUDA(cudaEventRecord(m.wide_ready, stream));
 }
 
 void sddmm_launch(const Matrix& m, int N, const float* lhs, const float* rhs, float* const* out,
                   cudaStream_t stream) {
-  if (m.num_tasks == 0) return;
+  const TaskOrder o = order_for(N);
+  if (m.num_tasks[o] == 0) return;
   SddmmArgs a{};
   a.ws = view_of(m);
   for (int s = 0; s < m.S; ++s) a.out_ws[s] = out[s];
-  a.tasks = m.tasks;
-  a.num_tasks = m.num_tasks;
+  a.tasks = m.tasks[o];
+  a.num_tasks = m.num_tasks[o];
   a.res_row = m.residue_row;
   a.lhs = lhs;
   a.rhs = rhs;
   if (N == 128) {
-    sddmm_fused<16, 2, 4><<<task_blocks(m.num_tasks, 16), kThreads, 0, stream>>>(a);
+    sddmm_fused<16, 2, 4><<<task_blocks(a.num_tasks, 16), kThreads, 0, stream>>>(a);
   } else {
-    sddmm_fused<8, 1, 8><<<task_blocks(m.num_tasks, 8), kThreads, 0, stream>>>(a);
+    sddmm_fused<8, 1, 8><<<task_blocks(a.num_tasks, 8), kThreads, 0, stream>>>(a);
   }
   PSB_LAUNCH_CHECK();
 }

@@ -114,6 +114,53 @@ def test_spmm_accumulates_like_the_reference_when_not_zeroed():
     _assert_close(twice[~stored], 2 * once[~stored].astype(np.float64), "atomic rows")
 
 
+def _heavy_rows_matrix(seed: int):
+    """Light Chung-Lu rows plus four rows of 2100-3600 nnz (wide rows: >= 8 block slices)."""
+    base = synth.chung_lu(4000, 12, 300, 2.1, seed=seed)
+    rng = np.random.default_rng(seed)
+    rows, ptr, cols, vals = [], [0], [], []
+    for r in range(base.rows):
+        lo, hi = base.row_ptr[r], base.row_ptr[r + 1]
+        c, v = list(base.col_ind[lo:hi]), list(base.values[lo:hi])
+        if r % 1000 == 3:
+            extra = rng.choice(base.cols, size=2100 + 500 * (r // 1000), replace=False)
+            merged = dict(zip(c, v))
+            for x in extra:
+                merged.setdefault(int(x), float(rng.uniform(-1, 1)))
+            c, v = sorted(merged), [merged[k] for k in sorted(merged)]
+        cols += c
+        vals += v
+        ptr.append(len(cols))
+    return synth.Csr(base.rows, base.cols, np.array(ptr, np.int32), np.array(cols, np.int32),
+                     np.array(vals, np.float32), False)
+
+
+def test_spmm_wide_rows_sum_in_fp64():
+    """Wide rows go through the FP64 scratch: results match the oracle at both task orders
+    (N = 32 and 128), a second call without zeroing C doubles them (the scratch is zero
+    again after each call), and growing N reallocates the scratch."""
+    mtx = _heavy_rows_matrix(21)
+    L = oracle.build_layout(mtx.rows, mtx.cols, mtx.row_ptr, mtx.col_ind, mtx.values, 1)
+    stored = np.zeros(mtx.rows, dtype=bool)  # single-group residue rows are stored, not added
+    for g in range(L.group_num[0]):
+        if not L.residue_atomic[g]:
+            stored[L.group_des[0][g]] = True
+    exp = {}
+    with psb.PowerSparseMatrixGPU(mtx.rows, mtx.cols, mtx.nnz, mtx.row_ptr, mtx.col_ind, mtx.values,
+                                  sm_count=1) as m:
+        assert m.wide_rows == 4
+        for n in (32, 128, 32, 256):
+            B = synth.dense(mtx.cols, n, 40 + n)
+            if n not in exp:
+                exp[n] = oracle.spmm(mtx.row_ptr, mtx.col_ind, mtx.values, B)
+            C = _spmm(m, B)
+            _assert_close(C.cpu().numpy(), exp[n], f"N={n}")
+            psb.SpMM(m, n, torch.from_numpy(B).cuda(), C)
+            torch.cuda.synchronize()
+            twice = np.where(stored[:, None], exp[n], 2 * exp[n])
+            _assert_close(C.cpu().numpy(), twice, f"N={n} twice")
+
+
 def test_spmm_on_a_side_stream():
     mtx = synth.chung_lu(2000, 20, 400, 2.1, seed=12)
     with psb.PowerSparseMatrixGPU(mtx.rows, mtx.cols, mtx.nnz, mtx.row_ptr, mtx.col_ind, mtx.values,
