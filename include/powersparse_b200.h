@@ -100,6 +100,21 @@ int ps_matrix_wide_rows(const ps_matrix* matrix);
  * (utils/matrix_utils.h:72-76) does not apply. */
 int ps_spmm(const ps_matrix* matrix, int N, const float* B, float* C, void* stream);
 
+/* ps_spmm that allocates no device memory.  No counterpart in the reference.
+ * For callers that cannot allocate while they run: engines that reserve the
+ * GPU's memory up front and serve it from their own pool, and latency-bound
+ * callers that cannot take the synchronization cudaMalloc / cudaFree may imply.
+ * ps_spmm keeps an FP64 scratch for wide rows (ps_matrix_wide_rows) in the
+ * matrix and grows it with cudaMalloc when N grows; this entry point uses a
+ * fixed 16 MiB device array instead (2^21 doubles, held by every GPU that
+ * loads the library until exit) and fails with PS_ERR_INVALID_ARGUMENT when
+ * ps_matrix_wide_rows(matrix) * N exceeds 2^21.  Same inputs, outputs and
+ * results as ps_spmm.  The first call on a device resolves the array's device
+ * address; make that first call before any stream capture.  All calls share
+ * the array: calls that overlap on the GPU (other streams, other matrices)
+ * race and give wrong results. */
+int ps_spmm_noalloc(const ps_matrix* matrix, int N, const float* B, float* C, void* stream);
+
 /* FP32 SDDMM on `stream`, asynchronous: for every element e of workset s,
  * out[s][e] (+)= A_e * <lhs[row(e), :], rhs[col(e), :]>, outputs in workset order.
  * lhs is [MatrixRow() x N], rhs [MatrixCol() x N], row-major device arrays; `out`

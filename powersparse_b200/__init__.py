@@ -63,6 +63,7 @@ _SIGNATURES = [
     ("ps_matrix_device", ctypes.c_int, [_vp]),
     ("ps_matrix_wide_rows", ctypes.c_int, [_vp]),
     ("ps_spmm", ctypes.c_int, [_vp, ctypes.c_int, _vp, _vp, _vp]),
+    ("ps_spmm_noalloc", ctypes.c_int, [_vp, ctypes.c_int, _vp, _vp, _vp]),
     ("ps_sddmm", ctypes.c_int, [_vp, ctypes.c_int, _vp, _vp, ctypes.POINTER(_vp), _vp]),
     ("ps_partition_rows", ctypes.c_int, [ctypes.c_int, _i32p, ctypes.c_int, _i32p]),
 ]

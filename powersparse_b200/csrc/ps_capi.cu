@@ -113,6 +113,18 @@ int ps_spmm(const ps_matrix* h, int N, const float* B, float* C, void* stream) {
   });
 }
 
+int ps_spmm_noalloc(const ps_matrix* h, int N, const float* B, float* C, void* stream) {
+  return guarded([&] {
+    if (!h) throw std::invalid_argument("Invalid SpMM buffers or stream count");
+    if (N <= 0 || N % 32 != 0 || N / 32 > 65535)
+      throw std::invalid_argument("SpMM requires N to be a positive multiple of 32, with N/32 <= 65535");
+    if (!B || !C) throw std::invalid_argument("Invalid SpMM buffers or stream count");
+    const psb::Matrix& m = M(h);
+    require_device(m);
+    psb::spmm_launch_noalloc(m, N, B, C, static_cast<cudaStream_t>(stream));
+  });
+}
+
 int ps_sddmm(const ps_matrix* h, int N, const float* lhs, const float* rhs, float* const* out, void* stream) {
   return guarded([&] {
     // Same checks as PowerSparse_SDDMM/sddmm_solution.cu:10-22.

@@ -24,7 +24,10 @@
 #include "ps_ops.h"
 
 #include <algorithm>
+#include <mutex>
 #include <stdexcept>
+#include <string>
+#include <unordered_map>
 
 namespace psb {
 namespace {
@@ -512,6 +515,77 @@ void sddmm_launch(const Matrix& m, int N, const float* lhs, const float* rhs, fl
     sddmm_fused<8, 1, 8><<<task_blocks(a.num_tasks, 8), kThreads, 0, stream>>>(a);
   }
   PSB_LAUNCH_CHECK();
+}
+
+// --- SpMM without allocation (ps_spmm_noalloc) -------------------------------
+//
+// No counterpart in the reference.  For callers that must not allocate device
+// memory while they run: engines that reserve the GPU's memory up front and hand
+// it out from their own pool (a cudaMalloc at call time fails or escapes their
+// accounting), and latency-bound callers that cannot take the device-wide
+// synchronization cudaMalloc / cudaFree may imply.  spmm_launch keeps the FP64
+// wide-row scratch in the matrix and grows it with cudaMalloc when N grows; this
+// variant runs the same kernels with that scratch in a fixed array of this file,
+// which every GPU that loads the library holds until the process exits.
+static __device__ __align__(256) double g_noalloc_wide_acc[kNoAllocScratchDoubles];
+
+namespace {
+
+std::mutex g_noalloc_mutex;
+std::unordered_map<int, double*> g_noalloc_addr;  // device -> address of g_noalloc_wide_acc
+
+// Device address of the array on `device` (the current device), resolved once
+// per device.  The host-side name of the array is not a device address.
+double* noalloc_scratch(int device) {
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  const auto it = g_noalloc_addr.find(device);
+  if (it != g_noalloc_addr.end()) return it->second;
+  double* p = nullptr;
+  PSB_CUDA(cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_noalloc_wide_acc));
+  g_noalloc_addr.emplace(device, p);
+  return p;
+}
+
+}  // namespace
+
+void spmm_launch_noalloc(const Matrix& m, int N, const float* B, float* C, cudaStream_t stream) {
+  const long long need = (long long)m.wide_rows * N;
+  if (need > kNoAllocScratchDoubles)
+    throw std::invalid_argument("ps_spmm_noalloc: this matrix needs " + std::to_string(need) +
+                                " doubles of scratch at N=" + std::to_string(N) + " (" +
+                                std::to_string(m.wide_rows) + " wide rows x N), above the fixed " +
+                                std::to_string(kNoAllocScratchDoubles) + " (16 MiB); use ps_spmm");
+  const TaskOrder o = order_for(N);
+  if (m.num_tasks[o] == 0) return;
+  SpmmArgs a{};
+  a.ws = view_of(m);
+  a.tasks = m.tasks[o];
+  a.num_tasks = m.num_tasks[o];
+  a.res_off = m.residue_offset;
+  a.res_atomic = m.residue_atomic;
+  a.res_groups = m.group_num[0];
+  a.B = B;
+  a.C = C;
+  a.ldb = N;
+  if (m.wide_rows > 0) {
+    // The array keeps whatever the previous call (of any matrix) left in it.
+    a.wide_acc = noalloc_scratch(m.device);
+    PSB_CUDA(cudaMemsetAsync(a.wide_acc, 0, sizeof(double) * size_t(need), stream));
+  }
+  if (N % 128 == 0) {
+    spmm_fused<32><<<dim3(task_blocks(a.num_tasks, 32), N / 128), kThreads, 0, stream>>>(a);
+  } else if (N % 64 == 0) {
+    spmm_fused<16><<<dim3(task_blocks(a.num_tasks, 16), N / 64), kThreads, 0, stream>>>(a);
+  } else {
+    spmm_fused<8><<<dim3(task_blocks(a.num_tasks, 8), N / 32), kThreads, 0, stream>>>(a);
+  }
+  PSB_LAUNCH_CHECK();
+  if (m.wide_rows > 0) {
+    const long long total = (long long)m.wide_rows * (N / 4);
+    const unsigned blocks = unsigned(std::min<long long>((total + 255) / 256, 148LL * 8));
+    wide_rows_fold<<<blocks, 256, 0, stream>>>(m.wide_row, m.wide_rows, N, a.wide_acc, C);
+    PSB_LAUNCH_CHECK();
+  }
 }
 
 }  // namespace psb

@@ -10,6 +10,13 @@ namespace psb {
 // C[rows x N] (+)= A * B[cols x N]; N a positive multiple of 32.
 void spmm_launch(const Matrix& m, int N, const float* B, float* C, cudaStream_t stream);
 
+// spmm_launch with the wide-row scratch in a fixed device array instead of the
+// matrix's cudaMalloc'd buffer; allocates nothing.  Throws std::invalid_argument
+// when wide_rows * N exceeds kNoAllocScratchDoubles.  Calls that overlap on the
+// GPU share the array and race.
+constexpr long long kNoAllocScratchDoubles = 1LL << 21;  // 16 MiB
+void spmm_launch_noalloc(const Matrix& m, int N, const float* B, float* C, cudaStream_t stream);
+
 // out[s][e] (+)= A_e * <lhs[row(e)], rhs[col(e)]>; N is 32 or 128.
 void sddmm_launch(const Matrix& m, int N, const float* lhs, const float* rhs, float* const* out,
                   cudaStream_t stream);
