@@ -84,9 +84,17 @@ struct SpmmArgs {
 template <int LG>
 __global__ void __launch_bounds__(kThreads, 4) spmm_fused(const SpmmArgs a) {
   constexpr int NG = 32 / LG;
-  // (column, value bits) of the staged chunk; odd stride keeps lane groups on
-  // different banks.
-  __shared__ int2 s_cv[kWarpsPerBlock][NG][kChunk + 1];
+  // Column indices and values of the staged chunk, read back 4 at a time (one
+  // 16-byte shared load each); rows of kChunk + 4 words put the lane groups of a
+  // warp 4 banks apart.
+  // With one lane group per warp (LG = 32) pairs staged as int2 and read one
+  // element at a time measure faster (2-4% at N = 128 on B200).
+  constexpr bool kPairs = LG == 32;
+  constexpr int kStride = kChunk + 4;
+  static_assert(kUnroll == 4, "elements are read from shared memory 4 at a time");
+  __shared__ __align__(16) int s_col[kWarpsPerBlock][NG][kStride];
+  __shared__ __align__(16) float s_val[kWarpsPerBlock][NG][kStride];
+  __shared__ int2 s_cv[kPairs ? kWarpsPerBlock : 1][kChunk + 1];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q = lane / LG, l = lane % LG;
   const unsigned gm = LG == 32 ? 0xffffffffu : (((1u << LG) - 1u) << (q * LG));
@@ -99,14 +107,9 @@ __global__ void __launch_bounds__(kThreads, 4) spmm_fused(const SpmmArgs a) {
   const int colofs = blockIdx.y * (4 * LG) + l * 4;
   const float* __restrict__ Bl = a.B + colofs;
   float* __restrict__ Cl = a.C + colofs;
-  int2* cv = s_cv[warp][q];
-  auto stage = [&](int base, int n) {
-#pragma unroll
-    for (int r = 0; r < kChunk / LG; ++r) {
-      const int i = l + r * LG;
-      if (i < n) cv[i] = make_int2(__ldcs(col + base + i), __float_as_int(__ldcs(val + base + i)));
-    }
-  };
+  int* sc = s_col[warp][q];
+  float* sv = s_val[warp][q];
+  int2* cv = s_cv[kPairs ? warp : 0];
   auto gather = [&](int c) { return __ldg(reinterpret_cast<const float4*>(Bl + (long long)c * a.ldb)); };
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 
@@ -125,19 +128,40 @@ __global__ void __launch_bounds__(kThreads, 4) spmm_fused(const SpmmArgs a) {
     bool cur_atomic = __shfl_sync(gm, g_atomic, 0, LG);
     for (int base = t.begin; base < t.end; base += kChunk) {
       const int n = min(kChunk, t.end - base);
-      stage(base, n);
-      __syncwarp(gm);
-      for (int j = 0; j < n; j += kUnroll) {
-        float4 b[kUnroll];
-        float sv[kUnroll];
+      // Residue tasks start anywhere, so they are staged element by element.
 #pragma unroll
-        for (int u = 0; u < kUnroll; ++u) {
-          if (j + u < n) {
-            const int2 e = cv[j + u];
-            b[u] = gather(e.x);
-            sv[u] = __int_as_float(e.y);
+      for (int r = 0; r < kChunk / LG; ++r) {
+        const int i = l + r * LG;
+        if (i < n) {
+          if constexpr (kPairs) {
+            cv[i] = make_int2(__ldcs(col + base + i), __float_as_int(__ldcs(val + base + i)));
+          } else {
+            sc[i] = __ldcs(col + base + i);
+            sv[i] = __ldcs(val + base + i);
           }
         }
+      }
+      __syncwarp(gm);
+      for (int j = 0; j < n; j += kUnroll) {
+        int cc[kUnroll];
+        float vv[kUnroll];
+        if constexpr (kPairs) {
+#pragma unroll
+          for (int u = 0; u < kUnroll; ++u) {
+            const int2 e = cv[j + u];
+            cc[u] = e.x;
+            vv[u] = __int_as_float(e.y);
+          }
+        } else {
+          const int4 c4 = *reinterpret_cast<const int4*>(sc + j);
+          const float4 v4 = *reinterpret_cast<const float4*>(sv + j);
+          cc[0] = c4.x; cc[1] = c4.y; cc[2] = c4.z; cc[3] = c4.w;
+          vv[0] = v4.x; vv[1] = v4.y; vv[2] = v4.z; vv[3] = v4.w;
+        }
+        float4 b[kUnroll];
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u)
+          if (j + u < n) b[u] = gather(cc[u]);
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
           if (j + u < n) {
@@ -157,7 +181,7 @@ __global__ void __launch_bounds__(kThreads, 4) spmm_fused(const SpmmArgs a) {
               cur_row = __shfl_sync(gm, g_row, widx, LG);
               cur_atomic = __shfl_sync(gm, g_atomic, widx, LG);
             }
-            fma4(acc, sv[u], b[u]);
+            fma4(acc, vv[u], b[u]);
           }
         }
       }
@@ -173,20 +197,44 @@ __global__ void __launch_bounds__(kThreads, 4) spmm_fused(const SpmmArgs a) {
   int g = t.group;
   double dx = 0.0, dy = 0.0, dz = 0.0, dw = 0.0;
   for (int base = t.begin; base < t.end; base += kChunk) {
-    stage(base, kChunk);
+    // Block chunks start on 32-element (128-byte) boundaries: 8 lanes stage the
+    // 32 column indices with one 16-byte load each, 8 lanes the 32 values.
+    if constexpr (kPairs) {
+      cv[l] = make_int2(__ldcs(col + base + l), __float_as_int(__ldcs(val + base + l)));
+    } else if constexpr (LG == 8) {
+      *reinterpret_cast<int4*>(sc + 4 * l) = __ldcs(reinterpret_cast<const int4*>(col + base) + l);
+      *reinterpret_cast<float4*>(sv + 4 * l) = __ldcs(reinterpret_cast<const float4*>(val + base) + l);
+    } else if (l < 8) {
+      *reinterpret_cast<int4*>(sc + 4 * l) = __ldcs(reinterpret_cast<const int4*>(col + base) + l);
+    } else if (l < 16) {
+      *reinterpret_cast<float4*>(sv + 4 * (l - 8)) = __ldcs(reinterpret_cast<const float4*>(val + base) + (l - 8));
+    }
     __syncwarp(gm);
 #pragma unroll 1
     for (int j = 0; j < kChunk; j += kUnroll) {
       float4 b[kUnroll];
-      float sv[kUnroll];
+      if constexpr (kPairs) {
+        float vv[kUnroll];
 #pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        const int2 e = cv[j + u];
-        b[u] = gather(e.x);
-        sv[u] = __int_as_float(e.y);
+        for (int u = 0; u < kUnroll; ++u) {
+          const int2 e = cv[j + u];
+          b[u] = gather(e.x);
+          vv[u] = __int_as_float(e.y);
+        }
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) fma4(acc, vv[u], b[u]);
+      } else {
+        const int4 c4 = *reinterpret_cast<const int4*>(sc + j);
+        const float4 v4 = *reinterpret_cast<const float4*>(sv + j);
+        b[0] = gather(c4.x);
+        b[1] = gather(c4.y);
+        b[2] = gather(c4.z);
+        b[3] = gather(c4.w);
+        fma4(acc, v4.x, b[0]);
+        fma4(acc, v4.y, b[1]);
+        fma4(acc, v4.z, b[2]);
+        fma4(acc, v4.w, b[3]);
       }
-#pragma unroll
-      for (int u = 0; u < kUnroll; ++u) fma4(acc, sv[u], b[u]);
     }
     __syncwarp(gm);
     dx += acc.x; dy += acc.y; dz += acc.z; dw += acc.w;
