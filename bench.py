@@ -354,7 +354,9 @@ def main() -> None:
                        "nnz_total": nnz_total, "N": N, "S": m.GroupTypeNum(),
                        "parallelism": f"row-panel x{world}", "l2": "inputs larger than L2 (B >= 1.25 GB), no flush",
                        "preprocess_ms": round(m.preprocess_ms, 1)},
-            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps,
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+            # per step: spmm_fused, plus wide_rows_fold when the panel has wide rows
+            "gpu_launches": args.steps * (2 if m.wide_rows > 0 else 1),
             "clocks": clocks, "extra": extra,
         }
         print(json.dumps(line), flush=True)
