@@ -289,7 +289,24 @@ def main() -> None:
         extra[f"sddmm_n{n_sd}"] = {"ms": round(ms_sd, 4),
                                    "gflops": round(2.0 * nnz_total * n_sd / (ms_sd * 1e-3) / 1e9, 1),
                                    "roofline_frac": round(ab / (ms_sd * 1e-3) / 1e9 / peak, 4)}
-        del X, Y
+        # The same SDDMM with its output in CSR order (one fused launch), next to the
+        # unfused alternative: workset-order SDDMM, then a scatter through the map.
+        out_csr = torch.empty(panel.nnz, dtype=torch.float32, device=device)
+        ms_csr = timed(lambda: psb.SDDMM_csr(m, n_sd, X, Y, out_csr, stream), k_extra)
+        pos = [torch.as_tensor(psb._CudaArrayView(p, m.workset_size(s), "<i4"), device=device).long()
+               for s, p in enumerate(m.CsrPosition()) if m.workset_size(s) > 0]
+        src = [o[: m.workset_size(s)] for s, o in enumerate(outs) if m.workset_size(s) > 0]
+
+        def unfused():  # `stream` is torch's current stream, so the scatter follows in order
+            psb.SDDMM(m, n_sd, X, Y, outs, stream)
+            for p_s, o_s in zip(pos, src):
+                out_csr.index_copy_(0, p_s, o_s)
+
+        ms_unf = timed(unfused, k_extra)
+        extra[f"sddmm_csr_n{n_sd}"] = {"ms": round(ms_csr, 4),
+                                       "gflops": round(2.0 * nnz_total * n_sd / (ms_csr * 1e-3) / 1e9, 1),
+                                       "unfused_ms": round(ms_unf, 4)}
+        del X, Y, out_csr, pos, src
     del outs
 
     if args.gather:

@@ -60,6 +60,17 @@ int ps_matrix_create_sm(int row_num, int col_num, int nnz_num, const int* row_pt
  * Complete outstanding operator calls first.  NULL is ignored. */
 void ps_matrix_destroy(ps_matrix* matrix);
 
+/* Layout cache.  No reference counterpart: the reference preprocesses in every
+ * constructor.  ps_matrix_save writes the layout (the reference-visible arrays
+ * and the CSR position map) to `path`; ps_matrix_load reads it onto the current
+ * device, checks every index against the stored shape (a corrupt, truncated or
+ * foreign file is PS_ERR_INVALID_ARGUMENT and never reaches a kernel) and
+ * derives the rest, skipping the preprocessing.  The layout keeps the SM count it
+ * was built for (its S).  ps_matrix_preprocess_ms of a loaded matrix is the load
+ * time.  Synchronous. */
+int ps_matrix_save(const ps_matrix* matrix, const char* path);
+int ps_matrix_load(const char* path, ps_matrix** out);
+
 /* Accessors of utils/matrix_utils.h:30-40 (same meaning, same pointer kinds:
  * ps_matrix_group_num is a host array; the workset arrays are host arrays of
  * device pointers; residue offset / atomic flags are device arrays). */
@@ -74,6 +85,12 @@ const float* const* ps_matrix_workset_sp_data(const ps_matrix* matrix);    /* Wo
 const int* const* ps_matrix_group_destination(const ps_matrix* matrix);    /* GroupDestination() */
 const int* ps_matrix_residue_offset(const ps_matrix* matrix);              /* ResidueOffset()    */
 const bool* ps_matrix_residue_atomic(const ps_matrix* matrix);             /* ResidueAtomic()    */
+
+/* Host array of GroupTypeNum() device pointers: for workset s, the CSR position
+ * (index into the constructor's col_ind / sp_data) of each of its elements, in
+ * workset order.  No reference counterpart (the reference keeps no map back to
+ * the input order). */
+const int* const* ps_matrix_csr_position(const ps_matrix* matrix);
 
 /* Elements in workset s (residue: ResidueOffset()[GroupNum()[0]]; block s:
  * GroupNum()[s] * GROUP_SIZE(s)), as benchmarks/benchmark.cu:147-154 sizes the
@@ -125,6 +142,16 @@ int ps_spmm_noalloc(const ps_matrix* matrix, int N, const float* B, float* C, vo
  * PowerSparse_SDDMM/sddmm_solution.cu:7-50) with one fused launch. */
 int ps_sddmm(const ps_matrix* matrix, int N, const float* lhs, const float* rhs,
              float* const* out, void* stream);
+
+/* SDDMM with its output in the constructor's CSR order, asynchronous on `stream`:
+ * out[p] = sp_data[p] * <lhs[row(p), :], rhs[col_ind[p], :]> for p in [0, nnz),
+ * `out` a device array of MatrixNNZ() floats.  Every position is written once
+ * (a store, so `out` needs no zeroing).  N is 32 or 128.  No reference
+ * counterpart: the reference returns workset order only
+ * (PowerSparse_SDDMM/PowerSparse_SDDMM.h:12); this is the same fused kernel
+ * writing through ps_matrix_csr_position, with no separate permutation pass. */
+int ps_sddmm_csr(const ps_matrix* matrix, int N, const float* lhs, const float* rhs, float* out,
+                 void* stream);
 
 /* nnz-balanced contiguous row panels for `parts` GPUs: writes cuts[0..parts]
  * with cuts[0] = 0, cuts[parts] = row_num, nondecreasing, panel p = rows

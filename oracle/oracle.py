@@ -48,7 +48,7 @@ def lib():
         L.ps_oracle_workset_size.argtypes = [ctypes.c_void_p, ctypes.c_int]
         L.ps_oracle_workset_size.restype = ctypes.c_longlong
         for name, rt in (("col_ind", _i32p), ("sp_data", _f32p), ("group_des", _i32p),
-                         ("group_order", _i32p)):
+                         ("group_order", _i32p), ("csr_pos", _i32p)):
             f = getattr(L, f"ps_oracle_{name}")
             f.argtypes = [ctypes.c_void_p, ctypes.c_int]
             f.restype = rt
@@ -90,6 +90,7 @@ class Layout:
     residue_offset: np.ndarray
     residue_atomic: np.ndarray
     group_order: list   # per workset: source group index of each final group
+    csr_pos: list       # per workset int32: CSR position of each element
 
     def offsets(self, s: int) -> np.ndarray:
         """Start offsets (int64, length G+1) of the groups of workset ``s``."""
@@ -126,6 +127,7 @@ def build_layout(rows: int, cols: int, row_ptr, col_ind, values, sm_count: int) 
             residue_offset=_arr(L.ps_oracle_residue_offset(h), gn[0] + 1, np.int32),
             residue_atomic=_arr(L.ps_oracle_residue_atomic(h), gn[0], np.uint8),
             group_order=[_arr(L.ps_oracle_group_order(h, s), gn[s], np.int32) for s in range(S)],
+            csr_pos=[_arr(L.ps_oracle_csr_pos(h, s), sizes[s], np.int32) for s in range(S)],
         )
     finally:
         L.ps_oracle_free(h)

@@ -50,6 +50,7 @@ struct Layout {
   int S = 0, fine = 16, signature_len = 32;
   std::vector<int> group_num;                  // [S]
   std::vector<std::vector<int>> col_ind;       // [S][workset size]
+  std::vector<std::vector<int>> csr_pos;       // [S][workset size]: CSR position of each element
   std::vector<std::vector<float>> sp_data;     // [S][workset size]
   std::vector<std::vector<int>> group_des;     // [S][group_num[s]]
   std::vector<int> residue_offset;             // [G0 + 1], permuted order
@@ -212,6 +213,7 @@ Layout build(int rows, int cols, int nnz, const int* row_ptr, const int* col_ind
   // Final worksets: groups in signature order, each group's columns ascending
   // (ties keep the frequency order, which for equal columns is CSR order).
   L.col_ind.assign(S, {});
+  L.csr_pos.assign(S, {});
   L.sp_data.assign(S, {});
   L.group_des.assign(S, {});
   for (int s = 0; s < S; ++s) {
@@ -232,6 +234,7 @@ Layout build(int rows, int cols, int nnz, const int* row_ptr, const int* col_ind
                        [&](int a, int b) { return col_ind[a] < col_ind[b]; });
       for (int p : tmp) {
         dc.push_back(col_ind[p]);
+        L.csr_pos[s].push_back(p);
         dv.push_back(vals[p]);
       }
       L.group_des[s][i] = des[s][src];
@@ -282,6 +285,7 @@ long long ps_oracle_workset_size(const ps_oracle_layout* h, int s) {
   return static_cast<long long>(L_.col_ind[s].size());
 }
 const int* ps_oracle_col_ind(const ps_oracle_layout* h, int s) { return L_.col_ind[s].data(); }
+const int* ps_oracle_csr_pos(const ps_oracle_layout* h, int s) { return L_.csr_pos[s].data(); }
 const float* ps_oracle_sp_data(const ps_oracle_layout* h, int s) { return L_.sp_data[s].data(); }
 const int* ps_oracle_group_des(const ps_oracle_layout* h, int s) { return L_.group_des[s].data(); }
 const int* ps_oracle_residue_offset(const ps_oracle_layout* h) { return L_.residue_offset.data(); }

@@ -24,7 +24,7 @@ from typing import Optional, Sequence
 import numpy as np
 
 __all__ = [
-    "PowerSparseMatrixGPU", "SpMM", "SDDMM", "partition_rows", "load_library", "LIB_PATH",
+    "PowerSparseMatrixGPU", "SpMM", "SDDMM", "SDDMM_csr", "partition_rows", "load_library", "LIB_PATH",
     "GROUP_SIZE", "PS_OK", "PS_ERR_INVALID_ARGUMENT", "PS_ERR_CUDA",
 ]
 
@@ -47,6 +47,8 @@ _SIGNATURES = [
     ("ps_matrix_create_sm", ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.c_int, _i32p, _i32p, _f32p,
                                            ctypes.c_int, ctypes.POINTER(_vp)]),
     ("ps_matrix_destroy", None, [_vp]),
+    ("ps_matrix_save", ctypes.c_int, [_vp, ctypes.c_char_p]),
+    ("ps_matrix_load", ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(_vp)]),
     ("ps_matrix_row", ctypes.c_int, [_vp]),
     ("ps_matrix_col", ctypes.c_int, [_vp]),
     ("ps_matrix_nnz", ctypes.c_int, [_vp]),
@@ -56,6 +58,7 @@ _SIGNATURES = [
     ("ps_matrix_workset_col_ind", ctypes.POINTER(_vp), [_vp]),
     ("ps_matrix_workset_sp_data", ctypes.POINTER(_vp), [_vp]),
     ("ps_matrix_group_destination", ctypes.POINTER(_vp), [_vp]),
+    ("ps_matrix_csr_position", ctypes.POINTER(_vp), [_vp]),
     ("ps_matrix_residue_offset", _vp, [_vp]),
     ("ps_matrix_residue_atomic", _vp, [_vp]),
     ("ps_matrix_workset_size", ctypes.c_longlong, [_vp, ctypes.c_int]),
@@ -65,6 +68,7 @@ _SIGNATURES = [
     ("ps_spmm", ctypes.c_int, [_vp, ctypes.c_int, _vp, _vp, _vp]),
     ("ps_spmm_noalloc", ctypes.c_int, [_vp, ctypes.c_int, _vp, _vp, _vp]),
     ("ps_sddmm", ctypes.c_int, [_vp, ctypes.c_int, _vp, _vp, ctypes.POINTER(_vp), _vp]),
+    ("ps_sddmm_csr", ctypes.c_int, [_vp, ctypes.c_int, _vp, _vp, _vp, _vp]),
     ("ps_partition_rows", ctypes.c_int, [ctypes.c_int, _i32p, ctypes.c_int, _i32p]),
 ]
 
@@ -146,6 +150,20 @@ class PowerSparseMatrixGPU:
                                        int(sm_count or 0), ctypes.byref(h)))
         self._h = h.value
 
+    # -- layout cache (ps_matrix_save / ps_matrix_load)
+    def save(self, path: str) -> None:
+        """Write the preprocessed layout to ``path`` (load it back with ``PowerSparseMatrixGPU.load``)."""
+        _check(load_library().ps_matrix_save(self.handle, os.fsencode(path)))
+
+    @classmethod
+    def load(cls, path: str) -> "PowerSparseMatrixGPU":
+        """A matrix from a layout file, on the current device, without preprocessing."""
+        h = _vp()
+        _check(load_library().ps_matrix_load(os.fsencode(path), ctypes.byref(h)))
+        self = cls.__new__(cls)
+        self._h = h.value
+        return self
+
     # -- lifetime
     def close(self) -> None:
         if self._h:
@@ -203,6 +221,10 @@ class PowerSparseMatrixGPU:
     def GroupDestination(self) -> list:
         return self._ptrs(load_library().ps_matrix_group_destination)
 
+    def CsrPosition(self) -> list:
+        """Per workset: device pointer to the CSR position of each element (ps_matrix_csr_position)."""
+        return self._ptrs(load_library().ps_matrix_csr_position)
+
     def ResidueOffset(self) -> int:
         return load_library().ps_matrix_residue_offset(self.handle) or 0
 
@@ -241,6 +263,7 @@ class PowerSparseMatrixGPU:
             out[f"ws{s}_col"] = _device_array(cols[s], n, torch.int32)
             out[f"ws{s}_val"] = _device_array(vals[s], n, torch.float32)
             out[f"ws{s}_des"] = _device_array(des[s], gn[s], torch.int32)
+            out[f"ws{s}_pos"] = _device_array(self.CsrPosition()[s], n, torch.int32)
         return out
 
 
@@ -275,6 +298,12 @@ def SDDMM(matrix: PowerSparseMatrixGPU, N: int, lhs, rhs, outputs: Sequence, str
     arr = (_vp * S)(*[_dev_ptr(o) for o in outputs])
     _check(load_library().ps_sddmm(matrix.handle, int(N), _dev_ptr(lhs), _dev_ptr(rhs), arr,
                                    _stream_ptr(stream)))
+
+
+def SDDMM_csr(matrix: PowerSparseMatrixGPU, N: int, lhs, rhs, out, stream=None) -> None:
+    """out[p] = A_p·<lhs[row(p)], rhs[col(p)]> in the constructor's CSR order (``out``: nnz floats)."""
+    _check(load_library().ps_sddmm_csr(matrix.handle, int(N), _dev_ptr(lhs), _dev_ptr(rhs), _dev_ptr(out),
+                                       _stream_ptr(stream)))
 
 
 def partition_rows(row_ptr, parts: int) -> np.ndarray:

@@ -74,6 +74,21 @@ int ps_matrix_create(int row_num, int col_num, int nnz_num, const int* row_ptr, 
 
 void ps_matrix_destroy(ps_matrix* matrix) { delete reinterpret_cast<psb::Matrix*>(matrix); }
 
+int ps_matrix_save(const ps_matrix* h, const char* path) {
+  return guarded([&] {
+    if (!h || !path) throw std::invalid_argument("ps_matrix_save: null matrix or path");
+    psb::save_matrix(M(h), path);
+  });
+}
+
+int ps_matrix_load(const char* path, ps_matrix** out) {
+  return guarded([&] {
+    if (!out || !path) throw std::invalid_argument("ps_matrix_load: null path or output handle");
+    *out = nullptr;
+    *out = reinterpret_cast<ps_matrix*>(psb::load_matrix(path));
+  });
+}
+
 int ps_matrix_row(const ps_matrix* h) { return M(h).rows; }
 int ps_matrix_col(const ps_matrix* h) { return M(h).cols; }
 int ps_matrix_nnz(const ps_matrix* h) { return M(h).nnz; }
@@ -88,6 +103,9 @@ const float* const* ps_matrix_workset_sp_data(const ps_matrix* h) {
 }
 const int* const* ps_matrix_group_destination(const ps_matrix* h) {
   return const_cast<const int* const*>(M(h).group_des.data());
+}
+const int* const* ps_matrix_csr_position(const ps_matrix* h) {
+  return const_cast<const int* const*>(M(h).csr_pos.data());
 }
 const int* ps_matrix_residue_offset(const ps_matrix* h) { return M(h).residue_offset; }
 const bool* ps_matrix_residue_atomic(const ps_matrix* h) { return M(h).residue_atomic; }
@@ -138,6 +156,17 @@ int ps_sddmm(const ps_matrix* h, int N, const float* lhs, const float* rhs, floa
     }
     require_device(m);
     psb::sddmm_launch(m, N, lhs, rhs, out, static_cast<cudaStream_t>(stream));
+  });
+}
+
+int ps_sddmm_csr(const ps_matrix* h, int N, const float* lhs, const float* rhs, float* out, void* stream) {
+  return guarded([&] {
+    if (N != 32 && N != 128)
+      throw std::invalid_argument("SDDMM dispatcher expects a benchmark width of N=32 or N=128");
+    if (!h || !lhs || !rhs || !out) throw std::invalid_argument("Invalid SDDMM buffers or stream count");
+    const psb::Matrix& m = M(h);
+    require_device(m);
+    psb::sddmm_csr_launch(m, N, lhs, rhs, out, static_cast<cudaStream_t>(stream));
   });
 }
 

@@ -27,7 +27,6 @@
 #include <memory>
 #include <numeric>
 #include <stdexcept>
-#include <unordered_map>
 
 namespace psb {
 
@@ -35,6 +34,7 @@ Matrix::~Matrix() {
   for (auto p : col_ind) cudaFree(p);
   for (auto p : sp_data) cudaFree(p);
   for (auto p : group_des) cudaFree(p);
+  for (auto p : csr_pos) cudaFree(p);
   cudaFree(residue_offset);
   cudaFree(residue_atomic);
   for (auto p : tasks) cudaFree(p);
@@ -255,11 +255,13 @@ __global__ void residue_rows(const int* __restrict__ res_off, const int* __restr
 
 __global__ void finalize_workset(const uint64_t* __restrict__ keys, const uint32_t* __restrict__ vals,
                                  long long n, uint64_t col_mask, const float* __restrict__ sp_data,
-                                 int* __restrict__ col_out, float* __restrict__ val_out) {
+                                 int* __restrict__ col_out, float* __restrict__ val_out,
+                                 int* __restrict__ pos_out) {
   for (long long q = blockIdx.x * (long long)blockDim.x + threadIdx.x; q < n;
        q += (long long)gridDim.x * blockDim.x) {
     col_out[q] = int(keys[q] & col_mask);
     val_out[q] = sp_data[vals[q]];
+    pos_out[q] = int(vals[q]);
   }
 }
 
@@ -373,6 +375,61 @@ std::vector<Task> build_tasks(const Matrix& m, const std::vector<int>& h_res_off
 }
 
 }  // namespace
+
+void finish_matrix(Matrix& mat, const std::vector<int>& h_res_off) {
+  Matrix* m = &mat;
+  const int S = m->S, G0 = m->group_num[0];
+  const int kBlocks = 148 * 16;
+  cudaStream_t st = nullptr;
+  if (m->ws_size[0] > 0) {
+    DeviceArray<int> rows_of(size_t(m->ws_size[0]));
+    residue_rows<<<grid_for(G0, 8, kBlocks), 256, 0, st>>>(m->residue_offset, m->group_des[0], G0, rows_of.get());
+    PSB_LAUNCH_CHECK();
+    m->residue_row = rows_of.release_ownership();
+  }
+
+  // Wide rows (kWideRowSlices): block slices per row, counted over the groups of
+  // the worksets whose groups are cut into slices; slots in row order.
+  std::vector<std::vector<int>> slot_of(S);
+  {
+    std::vector<std::vector<int>> h_des(S);
+    std::vector<int> slices(size_t(m->rows), 0);
+    for (int s = 1; s < S; ++s) {
+      const int G = group_size(s);
+      if (G < kTaskElems || m->group_num[s] == 0) continue;
+      h_des[s].resize(m->group_num[s]);
+      PSB_CUDA(cudaMemcpy(h_des[s].data(), m->group_des[s], sizeof(int) * h_des[s].size(), cudaMemcpyDeviceToHost));
+      for (int r : h_des[s]) slices[r] += G / kTaskElems;
+    }
+    std::vector<int> slot_of_row(size_t(m->rows), -1), h_wide_row;
+    for (int r = 0; r < m->rows; ++r) {
+      if (slices[r] >= kWideRowSlices) {
+        slot_of_row[r] = int(h_wide_row.size());
+        h_wide_row.push_back(r);
+      }
+    }
+    m->wide_rows = int(h_wide_row.size());
+    if (m->wide_rows > 0) {
+      for (int s = 1; s < S; ++s) {
+        if (h_des[s].empty()) continue;
+        slot_of[s].resize(h_des[s].size());
+        for (size_t g = 0; g < h_des[s].size(); ++g) slot_of[s][g] = slot_of_row[h_des[s][g]];
+      }
+      PSB_CUDA(cudaMalloc(reinterpret_cast<void**>(&m->wide_row), sizeof(int) * h_wide_row.size()));
+      PSB_CUDA(cudaMemcpy(m->wide_row, h_wide_row.data(), sizeof(int) * h_wide_row.size(), cudaMemcpyHostToDevice));
+      PSB_CUDA(cudaEventCreateWithFlags(&m->wide_ready, cudaEventDisableTiming));
+    }
+  }
+  for (int o = 0; o < kNumTaskOrders; ++o) {
+    const std::vector<Task> tasks = build_tasks(*m, h_res_off, TaskOrder(o), slot_of);
+    m->num_tasks[o] = int(tasks.size());
+    if (!tasks.empty()) {
+      PSB_CUDA(cudaMalloc(reinterpret_cast<void**>(&m->tasks[o]), sizeof(Task) * tasks.size()));
+      PSB_CUDA(cudaMemcpy(m->tasks[o], tasks.data(), sizeof(Task) * tasks.size(), cudaMemcpyHostToDevice));
+    }
+  }
+  PSB_CUDA(cudaDeviceSynchronize());
+}
 
 Matrix* build_matrix(int rows, int cols, int nnz, const int* row_ptr, const int* col_ind,
                      const float* sp_data, int sm_count) {
@@ -513,6 +570,7 @@ Matrix* build_matrix(int rows, int cols, int nnz, const int* row_ptr, const int*
   m->col_ind.assign(S, nullptr);
   m->sp_data.assign(S, nullptr);
   m->group_des.assign(S, nullptr);
+  m->csr_pos.assign(S, nullptr);
   m->ws_size.assign(S, 0);
   DeviceArray<int> res_off(size_t(G0) + 1);
   {
@@ -555,72 +613,19 @@ Matrix* build_matrix(int rows, int cols, int nnz, const int* row_ptr, const int*
     const int wg = bits_for(unsigned(G - 1));
     const bool alt = radix_sort_pairs<uint64_t>(keys.get(), vals.get(), keys_alt.get(), vals_alt.get(),
                                                 size_t(n), 0, wcol + wg, st);
-    DeviceArray<int> col_out(n);
+    DeviceArray<int> col_out(n), pos_out(n);
     DeviceArray<float> val_out(n);
     finalize_workset<<<grid_for(n, 256, kBlocks), 256, 0, st>>>(alt ? keys_alt.get() : keys.get(),
                                                                 alt ? vals_alt.get() : vals.get(), n,
                                                                 (uint64_t(1) << wcol) - 1, d_val.get(),
-                                                                col_out.get(), val_out.get());
+                                                                col_out.get(), val_out.get(), pos_out.get());
     PSB_LAUNCH_CHECK();
     m->col_ind[s] = col_out.release_ownership();
     m->sp_data[s] = val_out.release_ownership();
+    m->csr_pos[s] = pos_out.release_ownership();
   }
   m->residue_offset = res_off.release_ownership();
-  if (m->ws_size[0] > 0) {
-    DeviceArray<int> rows_of(size_t(m->ws_size[0]));
-    residue_rows<<<grid_for(G0, 8, kBlocks), 256, 0, st>>>(m->residue_offset, m->group_des[0], G0, rows_of.get());
-    PSB_LAUNCH_CHECK();
-    m->residue_row = rows_of.release_ownership();
-  }
-
-  // --- Tasks for the fused kernels.
-  // Wide rows (kWideRowSlices): block slices per row from its length, the same
-  // split into worksets as group_metadata makes; slots in row order.
-  std::vector<std::vector<int>> slot_of(S);
-  {
-    std::unordered_map<int, int> slot_of_row;
-    std::vector<int> h_wide_row;
-    for (int r = 0; r < rows && S > 1; ++r) {
-      int rest = row_ptr[r + 1] - row_ptr[r];
-      if (rest < kWideRowSlices * kTaskElems) continue;
-      long long slices = 0;
-      for (int s = S - 1; s >= 1; --s) {
-        const int G = group_size(s);
-        const int g = rest / G;
-        if (G >= kTaskElems) slices += (long long)g * (G / kTaskElems);
-        rest -= g * G;
-      }
-      if (slices >= kWideRowSlices) {
-        slot_of_row.emplace(r, int(h_wide_row.size()));
-        h_wide_row.push_back(r);
-      }
-    }
-    m->wide_rows = int(h_wide_row.size());
-    if (m->wide_rows > 0) {
-      for (int s = 1; s < S; ++s) {
-        if (group_size(s) < kTaskElems || m->group_num[s] == 0) continue;
-        std::vector<int> h_des(m->group_num[s]);
-        PSB_CUDA(cudaMemcpy(h_des.data(), m->group_des[s], sizeof(int) * h_des.size(), cudaMemcpyDeviceToHost));
-        slot_of[s].assign(h_des.size(), -1);
-        for (size_t g = 0; g < h_des.size(); ++g) {
-          const auto it = slot_of_row.find(h_des[g]);
-          if (it != slot_of_row.end()) slot_of[s][g] = it->second;
-        }
-      }
-      PSB_CUDA(cudaMalloc(reinterpret_cast<void**>(&m->wide_row), sizeof(int) * h_wide_row.size()));
-      PSB_CUDA(cudaMemcpy(m->wide_row, h_wide_row.data(), sizeof(int) * h_wide_row.size(), cudaMemcpyHostToDevice));
-      PSB_CUDA(cudaEventCreateWithFlags(&m->wide_ready, cudaEventDisableTiming));
-    }
-  }
-  for (int o = 0; o < kNumTaskOrders; ++o) {
-    const std::vector<Task> tasks = build_tasks(*m, h_res_off, TaskOrder(o), slot_of);
-    m->num_tasks[o] = int(tasks.size());
-    if (!tasks.empty()) {
-      PSB_CUDA(cudaMalloc(reinterpret_cast<void**>(&m->tasks[o]), sizeof(Task) * tasks.size()));
-      PSB_CUDA(cudaMemcpy(m->tasks[o], tasks.data(), sizeof(Task) * tasks.size(), cudaMemcpyHostToDevice));
-    }
-  }
-  PSB_CUDA(cudaDeviceSynchronize());
+  finish_matrix(*m, h_res_off);
   m->preprocess_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
   return m.release();
 }

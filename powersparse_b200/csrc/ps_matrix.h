@@ -5,6 +5,7 @@
 
 #include <cstdint>
 #include <mutex>
+#include <string>
 #include <vector>
 
 namespace psb {
@@ -52,6 +53,9 @@ struct Matrix {
   std::vector<long long> ws_size;      // elements per workset
   int* residue_offset = nullptr;       // device [G0 + 1]
   bool* residue_atomic = nullptr;      // device [G0], nullptr when G0 == 0
+  // CSR position (index into the constructor's col_ind / sp_data) of every
+  // workset element: SDDMM in CSR order writes through it.
+  std::vector<int*> csr_pos;           // device, per workset
 
   // Work decomposition for the fused SpMM / SDDMM kernels (not part of the
   // reference layout; derived from it).
@@ -80,12 +84,25 @@ struct Matrix {
   ~Matrix();
 };
 
+// Derives what the operators need beyond the reference layout (residue rows,
+// wide rows, both task orders) from a matrix whose layout arrays, group counts,
+// workset sizes and residue offsets (device, and h_res_off on the host) are set.
+// Used by build_matrix and by load_matrix.
+void finish_matrix(Matrix& m, const std::vector<int>& h_res_off);
+
 // Builds the layout on the current device from host CSR.  Throws
 // std::invalid_argument on an invalid CSR (same checks and messages as
 // utils/matrix_utils.cu:475-488) and psb::CudaError on CUDA failures.
 // sm_count <= 0 uses the device's multiprocessor count.
 Matrix* build_matrix(int rows, int cols, int nnz, const int* row_ptr, const int* col_ind,
                      const float* sp_data, int sm_count);
+
+// Layout cache (ps_cache.cu): writes the layout arrays to `path` / reads them
+// back onto the current device, validating every index, and derives the rest.
+// Errors: std::invalid_argument (unreadable, truncated or corrupt file),
+// std::runtime_error (write failure), psb::CudaError.
+void save_matrix(const Matrix& m, const std::string& path);
+Matrix* load_matrix(const std::string& path);
 
 // Task sizes in elements used by build_matrix.
 constexpr int kTaskElems = 256;

@@ -266,6 +266,8 @@ struct SddmmArgs {
   const float* lhs;
   const float* rhs;
   float* out_ws[kMaxWorksets];
+  const int* pos_ws[kMaxWorksets];  // CSR position of every element (CSR-order output)
+  float* out_csr;                   // CSR-order output, or nullptr
 };
 
 // Reduces BATCH per-lane partial dot products over the LG lanes of a lane group:
@@ -300,7 +302,9 @@ __device__ __forceinline__ float reduce_batch(float (&p)[BATCH], int l, unsigned
 // residue path loads each element's lhs row alongside its rhs row (per-element
 // rows from the matrix); block groups span whole 32-element chunks, so the block
 // path switches lhs rows once per chunk with the next group's row prefetched.
-template <int LG, int FC, int BATCH>
+// With kCsr every output goes to out_csr[csr_pos[e]] (a plain store: each CSR
+// position is written exactly once) instead of the workset-order buffers.
+template <int LG, int FC, int BATCH, bool kCsr = false>
 __global__ void __launch_bounds__(kThreads) sddmm_fused(const SddmmArgs a) {
   static_assert(BATCH <= LG && kChunk % BATCH == 0, "batch must fit the lane group and the chunk");
   constexpr int kLoadGroup = BATCH < kUnroll ? BATCH : kUnroll;  // gathers issued together
@@ -324,6 +328,7 @@ __global__ void __launch_bounds__(kThreads) sddmm_fused(const SddmmArgs a) {
   const int* __restrict__ col = a.ws.col[t.ws];
   const float* __restrict__ val = a.ws.val[t.ws];
   float* __restrict__ out = a.out_ws[t.ws];
+  const int* __restrict__ pos = a.pos_ws[t.ws];
   const float* __restrict__ rhs_l = a.rhs + 4 * l;
   const float* __restrict__ lhs_l = a.lhs + 4 * l;
   int* sc = s_col[warp][q];
@@ -384,7 +389,10 @@ __global__ void __launch_bounds__(kThreads) sddmm_fused(const SddmmArgs a) {
         }
         const float dot = reduce_batch<LG, BATCH>(p, l, gm);
         const int jl = j + l / kLanesPerElem;
-        if (l % kLanesPerElem == 0 && jl < n) atomicAdd(out + base + jl, dot * sv[jl]);
+        if (l % kLanesPerElem == 0 && jl < n) {
+          if constexpr (kCsr) a.out_csr[pos[base + jl]] = dot * sv[jl];
+          else atomicAdd(out + base + jl, dot * sv[jl]);
+        }
       }
       __syncwarp(gm);
     }
@@ -438,7 +446,10 @@ __global__ void __launch_bounds__(kThreads) sddmm_fused(const SddmmArgs a) {
       }
       const float dot = reduce_batch<LG, BATCH>(p, l, gm);
       const int jl = j + l / kLanesPerElem;
-      if (l % kLanesPerElem == 0) out[base + jl] = dot * sv[jl];
+      if (l % kLanesPerElem == 0) {
+        if constexpr (kCsr) a.out_csr[pos[base + jl]] = dot * sv[jl];
+        else out[base + jl] = dot * sv[jl];
+      }
     }
     __syncwarp(gm);
   }
@@ -561,6 +572,27 @@ void sddmm_launch(const Matrix& m, int N, const float* lhs, const float* rhs, fl
     sddmm_fused<16, 2, 4><<<task_blocks(a.num_tasks, 16), kThreads, 0, stream>>>(a);
   } else {
     sddmm_fused<8, 1, 8><<<task_blocks(a.num_tasks, 8), kThreads, 0, stream>>>(a);
+  }
+  PSB_LAUNCH_CHECK();
+}
+
+void sddmm_csr_launch(const Matrix& m, int N, const float* lhs, const float* rhs, float* out,
+                      cudaStream_t stream) {
+  const TaskOrder o = order_for(N);
+  if (m.num_tasks[o] == 0) return;
+  SddmmArgs a{};
+  a.ws = view_of(m);
+  for (int s = 0; s < m.S; ++s) a.pos_ws[s] = m.csr_pos[s];
+  a.out_csr = out;
+  a.tasks = m.tasks[o];
+  a.num_tasks = m.num_tasks[o];
+  a.res_row = m.residue_row;
+  a.lhs = lhs;
+  a.rhs = rhs;
+  if (N == 128) {
+    sddmm_fused<16, 2, 4, true><<<task_blocks(a.num_tasks, 16), kThreads, 0, stream>>>(a);
+  } else {
+    sddmm_fused<8, 1, 8, true><<<task_blocks(a.num_tasks, 8), kThreads, 0, stream>>>(a);
   }
   PSB_LAUNCH_CHECK();
 }

@@ -21,4 +21,9 @@ void spmm_launch_noalloc(const Matrix& m, int N, const float* B, float* C, cudaS
 void sddmm_launch(const Matrix& m, int N, const float* lhs, const float* rhs, float* const* out,
                   cudaStream_t stream);
 
+// out[p] = A_p * <lhs[row(p)], rhs[col(p)]> for every CSR position p of the
+// constructor's input (one store per element, no zeroing needed); N is 32 or 128.
+void sddmm_csr_launch(const Matrix& m, int N, const float* lhs, const float* rhs, float* out,
+                      cudaStream_t stream);
+
 }  // namespace psb

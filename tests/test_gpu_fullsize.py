@@ -78,3 +78,27 @@ def test_full_size_spmm_is_linear(cfg2):
     lhs, rhs = out[2], out[0] + 2 * out[1]
     scale = out[0].abs() + 2 * out[1].abs() + 1.0
     assert torch.all((lhs - rhs).abs() <= 1e-4 * scale)
+
+
+def test_full_size_sddmm_csr_order_is_the_permuted_workset_order(cfg2):
+    """CSR-order SDDMM equals the workset-order result moved through the position map,
+    bit for bit, and the map is a permutation of [0, nnz)."""
+    m, A = cfg2
+    pos = [torch.as_tensor(psb._CudaArrayView(A.CsrPosition()[s], A.workset_size(s), "<i4"), device="cuda")
+           for s in range(A.GroupTypeNum())]
+    allpos = torch.cat(pos)
+    assert torch.equal(torch.sort(allpos.long()).values, torch.arange(m.nnz, device="cuda"))
+    for n in (32, 128):
+        g = torch.Generator(device="cuda").manual_seed(n)
+        X = torch.rand((m.rows, n), generator=g, device="cuda")
+        Y = torch.rand((m.cols, n), generator=g, device="cuda")
+        out = torch.empty(m.nnz, device="cuda")
+        psb.SDDMM_csr(A, n, X, Y, out)
+        outs = [torch.zeros(max(A.workset_size(s), 1), device="cuda") for s in range(A.GroupTypeNum())]
+        psb.SDDMM(A, n, X, Y, outs)
+        moved = torch.empty(m.nnz, device="cuda")
+        for s in range(A.GroupTypeNum()):
+            moved[pos[s].long()] = outs[s][: A.workset_size(s)]
+        torch.cuda.synchronize()
+        # + 0 folds -0.0 into +0.0: residue outputs are added into zeros there.
+        assert torch.equal((out + 0).view(torch.int32), (moved + 0).view(torch.int32)), f"N={n}"

@@ -42,7 +42,9 @@ def test_layout_matches_reference_golden(name):
         assert m.GroupFineSize() == int(z["fine"])
         assert m.GroupNum() == [int(x) for x in z["group_num"]]
         got = m.download()
-    for key in [k for k in got if k.startswith(("ws", "res_"))]:
+    # The reference's layout arrays (the CSR position map has no reference counterpart;
+    # test_csr_positions_match_the_oracle covers it).
+    for key in [k for k in got if k.startswith(("ws", "res_")) and not k.endswith("_pos")]:
         if key in z.files:
             exp = z[key]
             if key.endswith("_val"):
@@ -117,3 +119,14 @@ def test_accessor_values():
         assert (m.MatrixRow(), m.MatrixCol(), m.MatrixNNZ()) == (rows, cols, len(ci))
         assert m.preprocess_ms > 0
         assert all(p != 0 for p, g in zip(m.WorksetColInd(), m.GroupNum()) if g)
+
+
+@pytest.mark.parametrize("name", golden_names())
+def test_csr_positions_match_the_oracle(name):
+    """The map back to CSR order (ps_matrix_csr_position) equals the oracle's."""
+    z, rows, cols, rp, ci, va, sm = load_golden(name)
+    L = oracle.build_layout(rows, cols, rp, ci, va, sm)
+    with _build(rows, cols, rp, ci, va, sm) as m:
+        got = m.download()
+    for s in range(L.S):
+        assert np.array_equal(got[f"ws{s}_pos"], L.csr_pos[s]), (name, s)

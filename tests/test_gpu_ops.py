@@ -74,6 +74,35 @@ def test_sddmm_matches_oracle_and_reference(name):
                     assert oracle.close(got[s], z[key], 1e-4, 1e-4).all()
 
 
+def _sddmm_csr_expected(rp, ci, va, X, Y):
+    """FP64 out[p] = val[p] * <X[row(p)], Y[col(p)]> in CSR order."""
+    rows = np.repeat(np.arange(len(rp) - 1), np.diff(rp))
+    return va.astype(np.float64) * np.einsum("ij,ij->i", X[rows].astype(np.float64), Y[ci].astype(np.float64))
+
+
+@pytest.mark.parametrize("name", golden_names())
+def test_sddmm_csr_order_matches_oracle_and_workset_order(name):
+    """SDDMM written in CSR order: within tolerance of the FP64 product and, bit for bit,
+    the workset-order result moved through the CSR position map."""
+    z, rows, cols, rp, ci, va, sm = load_golden(name)
+    with psb.PowerSparseMatrixGPU(rows, cols, len(ci), rp, ci, va, sm_count=sm) as m:
+        pos = m.download()
+        for n in (32, 128):
+            X, Y = dense_inputs(rows, n, 4000 + n), dense_inputs(cols, n, 5000 + n)
+            out = torch.full((len(ci),), float("nan"), device="cuda")
+            psb.SDDMM_csr(m, n, torch.from_numpy(X).cuda(), torch.from_numpy(Y).cuda(), out)
+            torch.cuda.synchronize()
+            got = out.cpu().numpy()
+            _assert_close(got, _sddmm_csr_expected(rp, ci, va, X, Y), f"{name} N={n}")
+            ws = _sddmm(m, X, Y)
+            moved = np.full(len(ci), np.nan, dtype=np.float32)
+            for s in range(m.GroupTypeNum()):
+                moved[pos[f"ws{s}_pos"]] = ws[s]
+            # + 0 folds -0.0 into +0.0: residue outputs are added into zeros there.
+            assert np.array_equal((got + np.float32(0)).view(np.uint32),
+                                  (moved + np.float32(0)).view(np.uint32)), f"{name} N={n}"
+
+
 @pytest.mark.parametrize("cfg,scale", [(2, 0.004), (3, 0.004), (4, 0.01)])
 @pytest.mark.parametrize("sm", [1, 148])
 def test_ops_on_scaled_configs(cfg, scale, sm):

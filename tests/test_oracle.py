@@ -106,6 +106,22 @@ def test_oracle_layout_is_a_permutation_of_the_csr(sm):
     assert np.array_equal(got[np.lexsort(got.T[::-1])], exp[np.lexsort(exp.T[::-1])])
 
 
+@pytest.mark.parametrize("name", golden_names())
+def test_oracle_csr_positions_map_back_to_the_csr(name):
+    """csr_pos is a permutation of [0, nnz) and every element reads its CSR entry:
+    same row (the group's destination), same column, same value bits."""
+    z, rows, cols, rp, ci, va, sm = load_golden(name)
+    L = oracle.build_layout(rows, cols, rp, ci, va, sm)
+    pos = np.concatenate([L.csr_pos[s] for s in range(L.S)])
+    assert np.array_equal(np.sort(pos), np.arange(len(ci)))
+    row_of = np.repeat(np.arange(rows), np.diff(rp))
+    for s in range(L.S):
+        p = L.csr_pos[s]
+        assert np.array_equal(ci[p], L.col_ind[s]), s
+        assert np.array_equal(va[p].view(np.uint32), L.sp_data[s].view(np.uint32)), s
+        assert np.array_equal(row_of[p], np.repeat(L.group_des[s], np.diff(L.offsets(s)))), s
+
+
 def test_oracle_rejects_invalid_csr_like_the_reference():
     rp = np.array([0, 1, 2], dtype=np.int32)
     with pytest.raises(ValueError, match="nonempty CSR"):
