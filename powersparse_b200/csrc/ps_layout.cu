@@ -37,7 +37,8 @@ Matrix::~Matrix() {
   for (auto p : csr_pos) cudaFree(p);
   cudaFree(residue_offset);
   cudaFree(residue_atomic);
-  for (auto p : tasks) cudaFree(p);
+  for (auto p : block_tasks) cudaFree(p);
+  for (auto p : residue_tasks) cudaFree(p);
   cudaFree(residue_row);
   cudaFree(wide_row);
   cudaFree(wide_acc);
@@ -324,22 +325,19 @@ void validate_csr(int rows, int cols, int nnz, const int* row_ptr, const int* co
       throw std::invalid_argument("Invalid CSR column index or sparse value");
 }
 
-// Splits every workset into tasks of about kTaskElems elements, largest group
-// sizes first (the reference launches worksets S-1 down to 0), in one of the
-// two orders of TaskOrder.
+// Block tasks of about kTaskElems elements, largest group sizes first (the
+// reference launches worksets S-1 down to 0), in one of the two BlockOrders.
 //
 // Why two orders (measured on B200, configurations 2-4): a row's most frequent
 // columns sit in its largest groups and each group's columns are ascending, so
 // slice k of the groups of one workset gathers from largely the same hot rows of
 // the dense operand.  Running those slices side by side (kSliceOrder) turns that
-// into L1/L2 hits when a dense row spans several cache lines (N >= 128: -4% to
-// -10% time).  With one-line rows (N = 32) the same order concentrates the
-// requests of every SM on a few lines at once and is slower, and there the
-// residue, which runs last, is cut finer so that the tail of the launch drains
-// quickly.
+// into L1/L2 hits when the dense operand does not fit L2 (N = 128: -4% to -10%
+// time; N = 32 on configurations 2-3: -1% to -3%).  When it does fit (config 4 at
+// N = 32), the same order concentrates the requests of every SM on a few lines at
+// once and row order is 6% faster.
 // `slot_of[s][g]`: wide-row slot of block group g of workset s (empty: none).
-std::vector<Task> build_tasks(const Matrix& m, const std::vector<int>& h_res_off, TaskOrder order,
-                              const std::vector<std::vector<int>>& slot_of) {
+std::vector<Task> build_block_tasks(const Matrix& m, BlockOrder order, const std::vector<std::vector<int>>& slot_of) {
   auto slot = [&](int s, int g) { return slot_of[s].empty() ? -1 : slot_of[s][g]; };
   std::vector<Task> tasks;
   for (int s = m.S - 1; s >= 1; --s) {
@@ -361,13 +359,20 @@ std::vector<Task> build_tasks(const Matrix& m, const std::vector<int>& h_res_off
       }
     }
   }
+  return tasks;
+}
+
+// Residue tasks: runs of whole residue groups of at most `elems` elements.  The
+// residue runs last in a launch; at N < 128 shorter tasks (kFineResidue) drain
+// that tail sooner (config 4 SpMM N = 32: -5%), at N >= 128 they cost ~3%.
+std::vector<Task> build_residue_tasks(const Matrix& m, const std::vector<int>& h_res_off, int elems) {
+  std::vector<Task> tasks;
   const int G0 = m.group_num[0];
-  const int residue_elems = order == kRowOrder ? kNarrowResidueTaskElems : kTaskElems;
   int g = 0;
   while (g < G0) {
     const int first = g;
     const int begin = h_res_off[g];
-    while (g < G0 && h_res_off[g + 1] - begin <= residue_elems) ++g;
+    while (g < G0 && h_res_off[g + 1] - begin <= elems) ++g;
     if (g == first) ++g;  // a single group longer than a task (cannot happen: <= 31 or 16)
     tasks.push_back({0, begin, h_res_off[g], first, -1});
   }
@@ -420,14 +425,21 @@ void finish_matrix(Matrix& mat, const std::vector<int>& h_res_off) {
       PSB_CUDA(cudaEventCreateWithFlags(&m->wide_ready, cudaEventDisableTiming));
     }
   }
-  for (int o = 0; o < kNumTaskOrders; ++o) {
-    const std::vector<Task> tasks = build_tasks(*m, h_res_off, TaskOrder(o), slot_of);
-    m->num_tasks[o] = int(tasks.size());
-    if (!tasks.empty()) {
-      PSB_CUDA(cudaMalloc(reinterpret_cast<void**>(&m->tasks[o]), sizeof(Task) * tasks.size()));
-      PSB_CUDA(cudaMemcpy(m->tasks[o], tasks.data(), sizeof(Task) * tasks.size(), cudaMemcpyHostToDevice));
-    }
-  }
+  auto upload_tasks = [](const std::vector<Task>& tasks, Task** dst, int* count) {
+    *count = int(tasks.size());
+    if (tasks.empty()) return;
+    PSB_CUDA(cudaMalloc(reinterpret_cast<void**>(dst), sizeof(Task) * tasks.size()));
+    PSB_CUDA(cudaMemcpy(*dst, tasks.data(), sizeof(Task) * tasks.size(), cudaMemcpyHostToDevice));
+  };
+  for (int o : {kRowOrder, kSliceOrder})
+    upload_tasks(build_block_tasks(*m, BlockOrder(o), slot_of), &m->block_tasks[o], &m->num_block_tasks[o]);
+  upload_tasks(build_residue_tasks(*m, h_res_off, kFineResidueTaskElems), &m->residue_tasks[kFineResidue],
+               &m->num_residue_tasks[kFineResidue]);
+  upload_tasks(build_residue_tasks(*m, h_res_off, kTaskElems), &m->residue_tasks[kCoarseResidue],
+               &m->num_residue_tasks[kCoarseResidue]);
+  int l2 = 0;
+  PSB_CUDA(cudaDeviceGetAttribute(&l2, cudaDevAttrL2CacheSize, m->device));
+  m->l2_bytes = l2;
   PSB_CUDA(cudaDeviceSynchronize());
 }
 

@@ -28,13 +28,14 @@ struct Task {
   int slot;
 };
 
-// The same tasks in two orders (build_matrix makes both; the operators pick one
-// by the width of a dense row):
-//   kRowOrder    slices of one group consecutive, residue tasks of at most
-//                kNarrowResidueTaskElems elements.  For rows of < 512 bytes.
-//   kSliceOrder  per workset, slice k of every group before slice k+1, residue
-//                tasks of at most kTaskElems elements.  For rows of >= 512 bytes.
-enum TaskOrder { kRowOrder = 0, kSliceOrder = 1, kNumTaskOrders = 2 };
+// A launch runs the block tasks (largest groups first), then the residue tasks.
+// Each part is kept in two variants and the operators combine one of each:
+//   block order   kRowOrder    a group's slices consecutive;
+//                 kSliceOrder  per workset, slice k of every group before slice k+1;
+//   residue cut   kFineResidue tasks of at most kFineResidueTaskElems elements;
+//                 kCoarseResidue at most kTaskElems.
+enum BlockOrder { kRowOrder = 0, kSliceOrder = 1 };
+enum ResidueCut { kFineResidue = 0, kCoarseResidue = 1 };
 
 struct Matrix {
   int device = 0;
@@ -59,9 +60,12 @@ struct Matrix {
 
   // Work decomposition for the fused SpMM / SDDMM kernels (not part of the
   // reference layout; derived from it).
-  // Per order: device tasks, block worksets (largest groups first), then the residue.
-  Task* tasks[kNumTaskOrders] = {};
-  int num_tasks[kNumTaskOrders] = {};
+  // Device task lists: block tasks per BlockOrder, residue tasks per ResidueCut.
+  Task* block_tasks[2] = {};
+  int num_block_tasks[2] = {};
+  Task* residue_tasks[2] = {};
+  int num_residue_tasks[2] = {};
+  long long l2_bytes = 0;              // L2 size of the device (picks the block order)
   // Destination row of every residue element (residue groups are short, so SDDMM
   // reads the lhs row per element instead of switching rows at group boundaries).
   int* residue_row = nullptr;          // device [ws_size[0]]
@@ -85,7 +89,7 @@ struct Matrix {
 };
 
 // Derives what the operators need beyond the reference layout (residue rows,
-// wide rows, both task orders) from a matrix whose layout arrays, group counts,
+// wide rows, the task lists) from a matrix whose layout arrays, group counts,
 // workset sizes and residue offsets (device, and h_res_off on the host) are set.
 // Used by build_matrix and by load_matrix.
 void finish_matrix(Matrix& m, const std::vector<int>& h_res_off);
@@ -106,7 +110,7 @@ Matrix* load_matrix(const std::string& path);
 
 // Task sizes in elements used by build_matrix.
 constexpr int kTaskElems = 256;
-constexpr int kNarrowResidueTaskElems = 64;
+constexpr int kFineResidueTaskElems = 64;
 // Rows with at least this many block slices are wide rows (FP64 slice sums).
 // A slice partial is rounded once per FP32 add into C; with k adds of a running
 // sum of magnitude R the rounding drift is about sqrt(k) * 2^-24 * R, which for

@@ -64,7 +64,9 @@ __device__ __forceinline__ void emit4(float* dst, const float4& v, bool atomic) 
 
 struct SpmmArgs {
   WorksetView ws;
-  const Task* tasks;
+  const Task* block_tasks;  // tasks [0, num_block)
+  int num_block;
+  const Task* res_tasks;    // tasks [num_block, num_tasks)
   int num_tasks;
   const int* res_off;
   const bool* res_atomic;
@@ -100,7 +102,7 @@ __global__ void __launch_bounds__(kThreads, 4) spmm_fused(const SpmmArgs a) {
   const unsigned gm = LG == 32 ? 0xffffffffu : (((1u << LG) - 1u) << (q * LG));
   const int task_id = (blockIdx.x * kWarpsPerBlock + warp) * NG + q;
   if (task_id >= a.num_tasks) return;
-  const Task t = a.tasks[task_id];
+  const Task t = task_id < a.num_block ? a.block_tasks[task_id] : a.res_tasks[task_id - a.num_block];
   const int* __restrict__ col = a.ws.col[t.ws];
   const float* __restrict__ val = a.ws.val[t.ws];
   const int* __restrict__ des = a.ws.des[t.ws];
@@ -260,7 +262,9 @@ __global__ void __launch_bounds__(kThreads, 4) spmm_fused(const SpmmArgs a) {
 
 struct SddmmArgs {
   WorksetView ws;
-  const Task* tasks;
+  const Task* block_tasks;  // tasks [0, num_block)
+  int num_block;
+  const Task* res_tasks;    // tasks [num_block, num_tasks)
   int num_tasks;
   const int* res_row;   // destination row of every residue element
   const float* lhs;
@@ -304,8 +308,10 @@ __device__ __forceinline__ float reduce_batch(float (&p)[BATCH], int l, unsigned
 // path switches lhs rows once per chunk with the next group's row prefetched.
 // With kCsr every output goes to out_csr[csr_pos[e]] (a plain store: each CSR
 // position is written exactly once) instead of the workset-order buffers.
+// 8-lane groups (N = 32) fit 64 registers and run 4 CTAs per SM (-2% to -8% on B200
+// against 3); the 16-lane kernel would spill at that bound and runs 3 (80 registers).
 template <int LG, int FC, int BATCH, bool kCsr = false>
-__global__ void __launch_bounds__(kThreads) sddmm_fused(const SddmmArgs a) {
+__global__ void __launch_bounds__(kThreads, LG == 8 ? 4 : 3) sddmm_fused(const SddmmArgs a) {
   static_assert(BATCH <= LG && kChunk % BATCH == 0, "batch must fit the lane group and the chunk");
   constexpr int kLoadGroup = BATCH < kUnroll ? BATCH : kUnroll;  // gathers issued together
   // Reusing a residue element's lhs row for the next element of the same group
@@ -324,7 +330,7 @@ __global__ void __launch_bounds__(kThreads) sddmm_fused(const SddmmArgs a) {
   const unsigned gm = LG == 32 ? 0xffffffffu : (((1u << LG) - 1u) << (q * LG));
   const int task_id = (blockIdx.x * kWarpsPerBlock + warp) * NG + q;
   if (task_id >= a.num_tasks) return;
-  const Task t = a.tasks[task_id];
+  const Task t = task_id < a.num_block ? a.block_tasks[task_id] : a.res_tasks[task_id - a.num_block];
   const int* __restrict__ col = a.ws.col[t.ws];
   const float* __restrict__ val = a.ws.val[t.ws];
   float* __restrict__ out = a.out_ws[t.ws];
@@ -496,18 +502,27 @@ WorksetView view_of(const Matrix& m) {
   return v;
 }
 
-// Task order for dense rows of N floats (TaskOrder in ps_matrix.h).
-TaskOrder order_for(int N) { return N >= 128 ? kSliceOrder : kRowOrder; }
+// The task lists of a launch over dense rows of N floats (ps_matrix.h): slice-major
+// block order when the gathered operand (cols x N floats) is more than half the
+// L2, residue tasks of kFineResidueTaskElems below N = 128.  Returns false when
+// the matrix has no work.
+template <typename Args>
+bool set_tasks(Args& a, const Matrix& m, int N) {
+  const int o = (long long)m.cols * N * 4 > m.l2_bytes / 2 ? kSliceOrder : kRowOrder;
+  const int r = N < 128 ? kFineResidue : kCoarseResidue;
+  a.block_tasks = m.block_tasks[o];
+  a.num_block = m.num_block_tasks[o];
+  a.res_tasks = m.residue_tasks[r];
+  a.num_tasks = m.num_block_tasks[o] + m.num_residue_tasks[r];
+  return a.num_tasks > 0;
+}
 
 }  // namespace
 
 void spmm_launch(const Matrix& m, int N, const float* B, float* C, cudaStream_t stream) {
-  const TaskOrder o = order_for(N);
-  if (m.num_tasks[o] == 0) return;
   SpmmArgs a{};
+  if (!set_tasks(a, m, N)) return;
   a.ws = view_of(m);
-  a.tasks = m.tasks[o];
-  a.num_tasks = m.num_tasks[o];
   a.res_off = m.residue_offset;
   a.res_atomic = m.residue_atomic;
   a.res_groups = m.group_num[0];
@@ -558,13 +573,10 @@ void spmm_launch(const Matrix& m, int N, const float* B, float* C, cudaStream_t 
 
 void sddmm_launch(const Matrix& m, int N, const float* lhs, const float* rhs, float* const* out,
                   cudaStream_t stream) {
-  const TaskOrder o = order_for(N);
-  if (m.num_tasks[o] == 0) return;
   SddmmArgs a{};
+  if (!set_tasks(a, m, N)) return;
   a.ws = view_of(m);
   for (int s = 0; s < m.S; ++s) a.out_ws[s] = out[s];
-  a.tasks = m.tasks[o];
-  a.num_tasks = m.num_tasks[o];
   a.res_row = m.residue_row;
   a.lhs = lhs;
   a.rhs = rhs;
@@ -578,14 +590,11 @@ void sddmm_launch(const Matrix& m, int N, const float* lhs, const float* rhs, fl
 
 void sddmm_csr_launch(const Matrix& m, int N, const float* lhs, const float* rhs, float* out,
                       cudaStream_t stream) {
-  const TaskOrder o = order_for(N);
-  if (m.num_tasks[o] == 0) return;
   SddmmArgs a{};
+  if (!set_tasks(a, m, N)) return;
   a.ws = view_of(m);
   for (int s = 0; s < m.S; ++s) a.pos_ws[s] = m.csr_pos[s];
   a.out_csr = out;
-  a.tasks = m.tasks[o];
-  a.num_tasks = m.num_tasks[o];
   a.res_row = m.residue_row;
   a.lhs = lhs;
   a.rhs = rhs;
@@ -635,12 +644,9 @@ void spmm_launch_noalloc(const Matrix& m, int N, const float* B, float* C, cudaS
                                 " doubles of scratch at N=" + std::to_string(N) + " (" +
                                 std::to_string(m.wide_rows) + " wide rows x N), above the fixed " +
                                 std::to_string(kNoAllocScratchDoubles) + " (16 MiB); use ps_spmm");
-  const TaskOrder o = order_for(N);
-  if (m.num_tasks[o] == 0) return;
   SpmmArgs a{};
+  if (!set_tasks(a, m, N)) return;
   a.ws = view_of(m);
-  a.tasks = m.tasks[o];
-  a.num_tasks = m.num_tasks[o];
   a.res_off = m.residue_offset;
   a.res_atomic = m.residue_atomic;
   a.res_groups = m.group_num[0];
