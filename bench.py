@@ -309,7 +309,7 @@ def main() -> None:
         del X, Y, out_csr, pos, src
     del outs
 
-    if args.gather:
+    if args.gather and world > 1:
         # Replicated result: all-gather the C panels over NCCL (outside the timed steps).
         from powersparse_b200.distributed import allgather_rows
         full = allgather_rows(C, cuts)
