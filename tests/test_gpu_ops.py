@@ -190,6 +190,36 @@ def test_spmm_wide_rows_sum_in_fp64():
             _assert_close(C.cpu().numpy(), twice, f"N={n} twice")
 
 
+def test_spmm_wide_rows_from_two_streams():
+    """Two SpMM calls on one matrix with wide rows, issued on two streams without a
+    host sync in between: the matrix's FP64 scratch is shared, and the calls are
+    ordered on the device, so both results are right."""
+    mtx = _heavy_rows_matrix(22)
+    with psb.PowerSparseMatrixGPU(mtx.rows, mtx.cols, mtx.nnz, mtx.row_ptr, mtx.col_ind, mtx.values,
+                                  sm_count=1) as m:
+        assert m.wide_rows > 0
+        Bs = [synth.dense(mtx.cols, 128, 60 + k) for k in range(2)]
+        dB = [torch.from_numpy(b).cuda() for b in Bs]
+        dC = [torch.zeros((mtx.rows, 128), device="cuda") for _ in range(2)]
+        streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+        torch.cuda.synchronize()
+        for _ in range(3):
+            for k in range(2):
+                dC[k].zero_()
+                torch.cuda.synchronize()
+                psb.SpMM(m, 128, dB[k], dC[k], streams[k])
+                psb.SpMM(m, 128, dB[k], dC[k], streams[1 - k])
+            torch.cuda.synchronize()
+        for k in range(2):
+            exp = oracle.spmm(mtx.row_ptr, mtx.col_ind, mtx.values, Bs[k])
+            L = oracle.build_layout(mtx.rows, mtx.cols, mtx.row_ptr, mtx.col_ind, mtx.values, 1)
+            stored = np.zeros(mtx.rows, dtype=bool)
+            for g in range(L.group_num[0]):
+                if not L.residue_atomic[g]:
+                    stored[L.group_des[0][g]] = True
+            _assert_close(dC[k].cpu().numpy(), np.where(stored[:, None], exp, 2 * exp), f"stream {k}")
+
+
 def test_spmm_on_a_side_stream():
     mtx = synth.chung_lu(2000, 20, 400, 2.1, seed=12)
     with psb.PowerSparseMatrixGPU(mtx.rows, mtx.cols, mtx.nnz, mtx.row_ptr, mtx.col_ind, mtx.values,
