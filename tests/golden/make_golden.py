@@ -171,7 +171,9 @@ def main() -> None:
     if len(sys.argv) > 2 and sys.argv[1] == "--trim":
         trim_existing(sys.argv[2:])
         return
-    outdir = sys.argv[1] if len(sys.argv) > 1 else os.path.join(ROOT, "gpurun_out", "golden")
+    if len(sys.argv) < 2:
+        sys.exit("usage: make_golden.py OUTDIR   (run on a GPU host; copy OUTDIR/*.npz here)  |  --trim FILES")
+    outdir = sys.argv[1]
     work = os.path.join(outdir, "_work")
     os.makedirs(outdir, exist_ok=True)
     summary = [run_case(name, spec, work, outdir) for name, spec in cases().items()]
