@@ -308,6 +308,17 @@ def main() -> None:
                                        "unfused_ms": round(ms_unf, 4)}
         del X, Y, out_csr, pos, src
     del outs
+    # SpMM with per-call edge values (CSR order) and the edge softmax of the attention
+    # chain, on the same panel.
+    w_csr = torch.rand(panel.nnz, dtype=torch.float32, device=device)
+    C_v = torch.zeros_like(C)
+    ms_v = timed(lambda: psb.SpMM_values(m, N, w_csr, B, C_v, stream), k_extra)
+    extra[f"spmm_values_n{N}"] = {"ms": round(ms_v, 4),
+                                  "gflops": round(2.0 * nnz_total * N / (ms_v * 1e-3) / 1e9, 1)}
+    ms_sm = timed(lambda: psb.edge_softmax_csr(m, w_csr, stream), k_extra)
+    extra["edge_softmax"] = {"ms": round(ms_sm, 4),
+                             "gb_per_s": round(panel.nnz * 4 * 5 / (ms_sm * 1e-3) / 1e9, 1)}
+    del w_csr, C_v
 
     if args.gather and world > 1:
         # Replicated result: all-gather the C panels over NCCL (outside the timed steps).

@@ -153,6 +153,20 @@ int ps_sddmm(const ps_matrix* matrix, int N, const float* lhs, const float* rhs,
 int ps_sddmm_csr(const ps_matrix* matrix, int N, const float* lhs, const float* rhs, float* out,
                  void* stream);
 
+/* SpMM with per-call edge values: C (+)= A' * B, where A' has the matrix's sparsity
+ * and the entry at CSR position p is values[p] (device, MatrixNNZ() floats, the
+ * constructor's CSR order) instead of sp_data[p].  Same B, C, N and stream rules as
+ * ps_spmm.  With ps_sddmm_csr and ps_edge_softmax_csr it forms the attention chain
+ * out = softmax_rows(A ⊙ (X Yᵀ)) · B.  No reference counterpart. */
+int ps_spmm_values(const ps_matrix* matrix, int N, const float* values, const float* B, float* C,
+                   void* stream);
+
+/* In place, for every row r of the matrix: values[p] = exp(values[p] - m_r) /
+ * sum_q exp(values[q] - m_r) over the row's CSR positions (m_r the row maximum);
+ * empty rows are untouched.  values: device, MatrixNNZ() floats, CSR order.  The
+ * row structure is the matrix's own.  No reference counterpart. */
+int ps_edge_softmax_csr(const ps_matrix* matrix, float* values, void* stream);
+
 /* nnz-balanced contiguous row panels for `parts` GPUs: writes cuts[0..parts]
  * with cuts[0] = 0, cuts[parts] = row_num, nondecreasing, panel p = rows
  * [cuts[p], cuts[p+1]).  Cut p is the first row whose row_ptr reaches

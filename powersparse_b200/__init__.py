@@ -24,7 +24,8 @@ from typing import Optional, Sequence
 import numpy as np
 
 __all__ = [
-    "PowerSparseMatrixGPU", "SpMM", "SDDMM", "SDDMM_csr", "partition_rows", "load_library", "LIB_PATH",
+    "PowerSparseMatrixGPU", "SpMM", "SDDMM", "SDDMM_csr", "SpMM_values", "edge_softmax_csr", "partition_rows",
+    "load_library", "LIB_PATH",
     "GROUP_SIZE", "PS_OK", "PS_ERR_INVALID_ARGUMENT", "PS_ERR_CUDA",
 ]
 
@@ -69,6 +70,8 @@ _SIGNATURES = [
     ("ps_spmm_noalloc", ctypes.c_int, [_vp, ctypes.c_int, _vp, _vp, _vp]),
     ("ps_sddmm", ctypes.c_int, [_vp, ctypes.c_int, _vp, _vp, ctypes.POINTER(_vp), _vp]),
     ("ps_sddmm_csr", ctypes.c_int, [_vp, ctypes.c_int, _vp, _vp, _vp, _vp]),
+    ("ps_spmm_values", ctypes.c_int, [_vp, ctypes.c_int, _vp, _vp, _vp, _vp]),
+    ("ps_edge_softmax_csr", ctypes.c_int, [_vp, _vp, _vp]),
     ("ps_partition_rows", ctypes.c_int, [ctypes.c_int, _i32p, ctypes.c_int, _i32p]),
 ]
 
@@ -304,6 +307,17 @@ def SDDMM_csr(matrix: PowerSparseMatrixGPU, N: int, lhs, rhs, out, stream=None) 
     """out[p] = A_p·<lhs[row(p)], rhs[col(p)]> in the constructor's CSR order (``out``: nnz floats)."""
     _check(load_library().ps_sddmm_csr(matrix.handle, int(N), _dev_ptr(lhs), _dev_ptr(rhs), _dev_ptr(out),
                                        _stream_ptr(stream)))
+
+
+def SpMM_values(matrix: PowerSparseMatrixGPU, N: int, values, B, C, stream=None) -> None:
+    """C (+)= A'·B with per-call edge values ``values`` (nnz floats, CSR order) in A's pattern."""
+    _check(load_library().ps_spmm_values(matrix.handle, int(N), _dev_ptr(values), _dev_ptr(B), _dev_ptr(C),
+                                         _stream_ptr(stream)))
+
+
+def edge_softmax_csr(matrix: PowerSparseMatrixGPU, values, stream=None) -> None:
+    """In place: softmax over each row's edge values (nnz floats, CSR order)."""
+    _check(load_library().ps_edge_softmax_csr(matrix.handle, _dev_ptr(values), _stream_ptr(stream)))
 
 
 def partition_rows(row_ptr, parts: int) -> np.ndarray:

@@ -159,6 +159,27 @@ int ps_sddmm(const ps_matrix* h, int N, const float* lhs, const float* rhs, floa
   });
 }
 
+int ps_spmm_values(const ps_matrix* h, int N, const float* values, const float* B, float* C, void* stream) {
+  return guarded([&] {
+    if (!h) throw std::invalid_argument("Invalid SpMM buffers or stream count");
+    if (N <= 0 || N % 32 != 0 || N / 32 > 65535)
+      throw std::invalid_argument("SpMM requires N to be a positive multiple of 32, with N/32 <= 65535");
+    if (!values || !B || !C) throw std::invalid_argument("Invalid SpMM buffers or stream count");
+    const psb::Matrix& m = M(h);
+    require_device(m);
+    psb::spmm_values_launch(m, N, values, B, C, static_cast<cudaStream_t>(stream));
+  });
+}
+
+int ps_edge_softmax_csr(const ps_matrix* h, float* values, void* stream) {
+  return guarded([&] {
+    if (!h || !values) throw std::invalid_argument("ps_edge_softmax_csr: null matrix or values");
+    const psb::Matrix& m = M(h);
+    require_device(m);
+    psb::edge_softmax_launch(m, values, static_cast<cudaStream_t>(stream));
+  });
+}
+
 int ps_sddmm_csr(const ps_matrix* h, int N, const float* lhs, const float* rhs, float* out, void* stream) {
   return guarded([&] {
     if (N != 32 && N != 128)

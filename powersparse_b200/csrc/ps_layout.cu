@@ -40,6 +40,7 @@ Matrix::~Matrix() {
   for (auto p : block_tasks) cudaFree(p);
   for (auto p : residue_tasks) cudaFree(p);
   cudaFree(residue_row);
+  cudaFree(row_ptr);
   cudaFree(wide_row);
   cudaFree(wide_acc);
   if (wide_ready) cudaEventDestroy(wide_ready);
@@ -244,6 +245,13 @@ __global__ void gather_group_elements(const uint32_t* __restrict__ order, int G,
   }
 }
 
+// lens[des[g]] += size of group g (group_len for block groups, from res_off for the residue).
+__global__ void add_group_lengths(const int* __restrict__ des, int groups, int group_len,
+                                  const int* __restrict__ res_off, int* __restrict__ lens) {
+  for (int g = blockIdx.x * blockDim.x + threadIdx.x; g < groups; g += gridDim.x * blockDim.x)
+    atomicAdd(&lens[des[g]], res_off ? res_off[g + 1] - res_off[g] : group_len);
+}
+
 __global__ void residue_rows(const int* __restrict__ res_off, const int* __restrict__ des, int groups,
                              int* __restrict__ row_of) {
   const int lane = threadIdx.x & 31;
@@ -386,6 +394,20 @@ void finish_matrix(Matrix& mat, const std::vector<int>& h_res_off) {
   const int S = m->S, G0 = m->group_num[0];
   const int kBlocks = 148 * 16;
   cudaStream_t st = nullptr;
+  if (!m->row_ptr) {
+    // A loaded layout: the row pointer from the group sizes of every row.
+    DeviceArray<int> lens(size_t(m->rows)), rp(size_t(m->rows) + 1);
+    PSB_CUDA(cudaMemsetAsync(lens.get(), 0, sizeof(int) * size_t(m->rows), st));
+    for (int s = 0; s < S; ++s) {
+      if (m->group_num[s] == 0) continue;
+      add_group_lengths<<<grid_for(m->group_num[s], 256, kBlocks), 256, 0, st>>>(
+          m->group_des[s], m->group_num[s], s == 0 ? 0 : group_size(s), s == 0 ? m->residue_offset : nullptr,
+          lens.get());
+      PSB_LAUNCH_CHECK();
+    }
+    exclusive_scan<int32_t>(lens.get(), rp.get(), size_t(m->rows), st);
+    m->row_ptr = rp.release_ownership();
+  }
   if (m->ws_size[0] > 0) {
     DeviceArray<int> rows_of(size_t(m->ws_size[0]));
     residue_rows<<<grid_for(G0, 8, kBlocks), 256, 0, st>>>(m->residue_offset, m->group_des[0], G0, rows_of.get());
@@ -637,6 +659,7 @@ Matrix* build_matrix(int rows, int cols, int nnz, const int* row_ptr, const int*
     m->csr_pos[s] = pos_out.release_ownership();
   }
   m->residue_offset = res_off.release_ownership();
+  m->row_ptr = d_row_ptr.release_ownership();
   finish_matrix(*m, h_res_off);
   m->preprocess_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
   return m.release();

@@ -54,6 +54,8 @@ struct Matrix {
   std::vector<long long> ws_size;      // elements per workset
   int* residue_offset = nullptr;       // device [G0 + 1]
   bool* residue_atomic = nullptr;      // device [G0], nullptr when G0 == 0
+  // Row pointer of the constructor's CSR (device, rows + 1): edge softmax rows.
+  int* row_ptr = nullptr;
   // CSR position (index into the constructor's col_ind / sp_data) of every
   // workset element: SDDMM in CSR order writes through it.
   std::vector<int*> csr_pos;           // device, per workset

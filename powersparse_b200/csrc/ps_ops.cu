@@ -75,6 +75,8 @@ struct SpmmArgs {
   float* C;
   long long ldb;  // N
   double* wide_acc;  // [wide rows][N] FP64 slice sums (tasks with slot >= 0)
+  const int* pos_ws[kMaxWorksets];  // CSR position of every element (kValues)
+  const float* values;              // per-call values in CSR order (kValues)
 };
 
 // SpMM, one task per lane group:
@@ -83,7 +85,9 @@ struct SpmmArgs {
 // their row has other groups, as in spmm_kernel_block.cu:155-161 and
 // spmm_kernel_residue.cu:68-81 of the reference.  Block groups accumulate FP32
 // per 32-element chunk and carry the running sum in FP64.
-template <int LG>
+// With kValues the value of element e is a.values[csr_pos[e]] (values supplied per
+// call in CSR order) instead of the layout's sp_data[e].
+template <int LG, bool kValues = false>
 __global__ void __launch_bounds__(kThreads, 4) spmm_fused(const SpmmArgs a) {
   constexpr int NG = 32 / LG;
   // Column indices and values of the staged chunk, read back 4 at a time (one
@@ -113,6 +117,19 @@ __global__ void __launch_bounds__(kThreads, 4) spmm_fused(const SpmmArgs a) {
   float* sv = s_val[warp][q];
   int2* cv = s_cv[kPairs ? warp : 0];
   auto gather = [&](int c) { return __ldg(reinterpret_cast<const float4*>(Bl + (long long)c * a.ldb)); };
+  const int* __restrict__ pos = a.pos_ws[t.ws];
+  auto value1 = [&](int e) -> float {
+    if constexpr (kValues) return __ldg(a.values + __ldcs(pos + e));
+    else return __ldcs(val + e);
+  };
+  auto value4 = [&](int e0, int k) -> float4 {  // elements e0 + 4k .. e0 + 4k + 3, e0 16-byte aligned
+    if constexpr (kValues) {
+      const int4 p = __ldcs(reinterpret_cast<const int4*>(pos + e0) + k);
+      return make_float4(__ldg(a.values + p.x), __ldg(a.values + p.y), __ldg(a.values + p.z), __ldg(a.values + p.w));
+    } else {
+      return __ldcs(reinterpret_cast<const float4*>(val + e0) + k);
+    }
+  };
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 
   if (t.ws == 0) {
@@ -136,10 +153,10 @@ __global__ void __launch_bounds__(kThreads, 4) spmm_fused(const SpmmArgs a) {
         const int i = l + r * LG;
         if (i < n) {
           if constexpr (kPairs) {
-            cv[i] = make_int2(__ldcs(col + base + i), __float_as_int(__ldcs(val + base + i)));
+            cv[i] = make_int2(__ldcs(col + base + i), __float_as_int(value1(base + i)));
           } else {
             sc[i] = __ldcs(col + base + i);
-            sv[i] = __ldcs(val + base + i);
+            sv[i] = value1(base + i);
           }
         }
       }
@@ -202,14 +219,14 @@ __global__ void __launch_bounds__(kThreads, 4) spmm_fused(const SpmmArgs a) {
     // Block chunks start on 32-element (128-byte) boundaries: 8 lanes stage the
     // 32 column indices with one 16-byte load each, 8 lanes the 32 values.
     if constexpr (kPairs) {
-      cv[l] = make_int2(__ldcs(col + base + l), __float_as_int(__ldcs(val + base + l)));
+      cv[l] = make_int2(__ldcs(col + base + l), __float_as_int(value1(base + l)));
     } else if constexpr (LG == 8) {
       *reinterpret_cast<int4*>(sc + 4 * l) = __ldcs(reinterpret_cast<const int4*>(col + base) + l);
-      *reinterpret_cast<float4*>(sv + 4 * l) = __ldcs(reinterpret_cast<const float4*>(val + base) + l);
+      *reinterpret_cast<float4*>(sv + 4 * l) = value4(base, l);
     } else if (l < 8) {
       *reinterpret_cast<int4*>(sc + 4 * l) = __ldcs(reinterpret_cast<const int4*>(col + base) + l);
     } else if (l < 16) {
-      *reinterpret_cast<float4*>(sv + 4 * (l - 8)) = __ldcs(reinterpret_cast<const float4*>(val + base) + (l - 8));
+      *reinterpret_cast<float4*>(sv + 4 * (l - 8)) = value4(base, l - 8);
     }
     __syncwarp(gm);
 #pragma unroll 1
@@ -485,6 +502,30 @@ __global__ void __launch_bounds__(256) wide_rows_fold(const int* __restrict__ wi
   }
 }
 
+// In-place softmax over each row's entries of a CSR-order array (one warp per row):
+// v[p] = exp(v[p] - max_row) / sum_row exp(v[q] - max_row).
+__global__ void __launch_bounds__(256) edge_softmax_rows(const int* __restrict__ row_ptr, int rows,
+                                                         float* __restrict__ v) {
+  const int lane = threadIdx.x & 31;
+  const int warps = (gridDim.x * blockDim.x) >> 5;
+  for (int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < rows; r += warps) {
+    const int b = row_ptr[r], e = row_ptr[r + 1];
+    if (b == e) continue;
+    float mx = -INFINITY;
+    for (int p = b + lane; p < e; p += 32) mx = fmaxf(mx, v[p]);
+    for (int d = 16; d > 0; d >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, d));
+    float sum = 0.f;
+    for (int p = b + lane; p < e; p += 32) {
+      const float x = expf(v[p] - mx);
+      v[p] = x;
+      sum += x;
+    }
+    for (int d = 16; d > 0; d >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, d);
+    const float inv = 1.f / sum;
+    for (int p = b + lane; p < e; p += 32) v[p] *= inv;
+  }
+}
+
 unsigned task_blocks(int num_tasks, int lane_group) {
   const long long per_block = (long long)kWarpsPerBlock * (32 / lane_group);
   return unsigned((num_tasks + per_block - 1) / per_block);
@@ -519,7 +560,12 @@ bool set_tasks(Args& a, const Matrix& m, int N) {
 
 }  // namespace
 
-void spmm_launch(const Matrix& m, int N, const float* B, float* C, cudaStream_t stream) {
+namespace {
+
+// SpMM with the layout's values (values == nullptr) or with per-call values in CSR
+// order (kValues).
+template <bool kValues>
+void spmm_run(const Matrix& m, int N, const float* B, float* C, const float* values, cudaStream_t stream) {
   SpmmArgs a{};
   if (!set_tasks(a, m, N)) return;
   a.ws = view_of(m);
@@ -529,13 +575,17 @@ void spmm_launch(const Matrix& m, int N, const float* B, float* C, cudaStream_t 
   a.B = B;
   a.C = C;
   a.ldb = N;
+  if constexpr (kValues) {
+    for (int s = 0; s < m.S; ++s) a.pos_ws[s] = m.csr_pos[s];
+    a.values = values;
+  }
   auto launch = [&] {
     if (N % 128 == 0) {
-      spmm_fused<32><<<dim3(task_blocks(a.num_tasks, 32), N / 128), kThreads, 0, stream>>>(a);
+      spmm_fused<32, kValues><<<dim3(task_blocks(a.num_tasks, 32), N / 128), kThreads, 0, stream>>>(a);
     } else if (N % 64 == 0) {
-      spmm_fused<16><<<dim3(task_blocks(a.num_tasks, 16), N / 64), kThreads, 0, stream>>>(a);
+      spmm_fused<16, kValues><<<dim3(task_blocks(a.num_tasks, 16), N / 64), kThreads, 0, stream>>>(a);
     } else {
-      spmm_fused<8><<<dim3(task_blocks(a.num_tasks, 8), N / 32), kThreads, 0, stream>>>(a);
+      spmm_fused<8, kValues><<<dim3(task_blocks(a.num_tasks, 8), N / 32), kThreads, 0, stream>>>(a);
     }
     PSB_LAUNCH_CHECK();
   };
@@ -569,6 +619,23 @@ void spmm_launch(const Matrix& m, int N, const float* B, float* C, cudaStream_t 
   wide_rows_fold<<<blocks, 256, 0, stream>>>(m.wide_row, m.wide_rows, N, m.wide_acc, C);
   PSB_LAUNCH_CHECK();
   if (capture == cudaStreamCaptureStatusNone) PSB_CUDA(cudaEventRecord(m.wide_ready, stream));
+}
+
+}  // namespace
+
+void spmm_launch(const Matrix& m, int N, const float* B, float* C, cudaStream_t stream) {
+  spmm_run<false>(m, N, B, C, nullptr, stream);
+}
+
+void spmm_values_launch(const Matrix& m, int N, const float* values, const float* B, float* C,
+                        cudaStream_t stream) {
+  spmm_run<true>(m, N, B, C, values, stream);
+}
+
+void edge_softmax_launch(const Matrix& m, float* values, cudaStream_t stream) {
+  const unsigned blocks = unsigned(std::max<long long>(1, std::min<long long>(((long long)m.rows + 7) / 8, 148LL * 16)));
+  edge_softmax_rows<<<blocks, 256, 0, stream>>>(m.row_ptr, m.rows, values);
+  PSB_LAUNCH_CHECK();
 }
 
 void sddmm_launch(const Matrix& m, int N, const float* lhs, const float* rhs, float* const* out,

@@ -10,6 +10,15 @@ namespace psb {
 // C[rows x N] (+)= A * B[cols x N]; N a positive multiple of 32.
 void spmm_launch(const Matrix& m, int N, const float* B, float* C, cudaStream_t stream);
 
+// C[rows x N] (+)= A' * B, A' with A's sparsity and the per-call values
+// `values[p]` (device, CSR order of the constructor's input) in place of sp_data.
+void spmm_values_launch(const Matrix& m, int N, const float* values, const float* B, float* C,
+                        cudaStream_t stream);
+
+// In place, for every row r: values[p] = softmax over p in [row_ptr[r], row_ptr[r+1])
+// (values: device, CSR order, MatrixNNZ() floats).
+void edge_softmax_launch(const Matrix& m, float* values, cudaStream_t stream);
+
 // spmm_launch with the wide-row scratch in a fixed device array instead of the
 // matrix's cudaMalloc'd buffer; allocates nothing.  Throws std::invalid_argument
 // when wide_rows * N exceeds kNoAllocScratchDoubles.  Calls that overlap on the
