@@ -149,7 +149,7 @@ __global__ void mark_positions(const int* __restrict__ pos, long long n, int nnz
   }
 }
 
-unsigned blocks_for(long long n) { return unsigned(std::max<long long>(1, std::min<long long>((n + 255) / 256, 148 * 8))); }
+unsigned blocks_for(long long n) { return unsigned(std::max<long long>(1, std::min<long long>((n + 255) / 256, 8LL * device_sms()))); }
 
 }  // namespace
 

@@ -3,6 +3,7 @@
 
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
 #include <stdexcept>
 #include <string>
@@ -28,6 +29,23 @@ inline void check_cuda(cudaError_t status, const char* expr, const char* file, i
 #define PSB_LAUNCH_CHECK() ::psb::check_cuda(cudaGetLastError(), "kernel launch", __FILE__, __LINE__)
 
 constexpr int kWarp = 32;
+
+// Multiprocessor count of the current device (cached per device): grid-stride
+// kernels launch a fixed number of CTAs per SM.
+inline int device_sms() {
+  static std::atomic<int> cache[64] = {};
+  int dev = 0;
+  PSB_CUDA(cudaGetDevice(&dev));
+  const bool cached = dev >= 0 && dev < 64;
+  if (cached) {
+    const int v = cache[dev].load(std::memory_order_relaxed);
+    if (v > 0) return v;
+  }
+  int v = 0;
+  PSB_CUDA(cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev));
+  if (cached) cache[dev].store(v, std::memory_order_relaxed);
+  return v;
+}
 
 __host__ __device__ inline int ceil_div(int a, int b) { return (a + b - 1) / b; }
 __host__ __device__ inline long long ceil_div_ll(long long a, long long b) { return (a + b - 1) / b; }

@@ -392,7 +392,7 @@ std::vector<Task> build_residue_tasks(const Matrix& m, const std::vector<int>& h
 void finish_matrix(Matrix& mat, const std::vector<int>& h_res_off) {
   Matrix* m = &mat;
   const int S = m->S, G0 = m->group_num[0];
-  const int kBlocks = 148 * 16;
+  const int kBlocks = 16 * device_sms();
   cudaStream_t st = nullptr;
   if (!m->row_ptr) {
     // A loaded layout: the row pointer from the group sizes of every row.
@@ -477,7 +477,7 @@ Matrix* build_matrix(int rows, int cols, int nnz, const int* row_ptr, const int*
   if (sm_count <= 0) PSB_CUDA(cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, m->device));
   m->sm_count = sm_count;
   cudaStream_t st = nullptr;  // preprocessing is synchronous, like the reference constructor
-  const int kBlocks = 148 * 16;
+  const int kBlocks = 16 * device_sms();
 
   DeviceArray<int> d_row_ptr(size_t(rows) + 1), d_col(nnz);
   DeviceArray<float> d_val(nnz);

@@ -14,11 +14,13 @@
 // are staged 32 at a time per lane group in shared memory and read back as
 // broadcasts; gathers are issued kUnroll at a time.
 //
-// Design note, from measurements on B200 (configurations 2 and 4): the gathers
-// are latency-bound, and the number of warps per SM matters more than the depth
-// of each warp's load batch, so the kernels are written to stay near 56-64
-// registers (4 CTAs of 256 threads per SM) with kUnroll = 4.  The residue and
-// block paths are separate code regions so their registers do not add up.
+// Design note, from measurements on B200 (configurations 2-4): the gathers are
+// latency-bound, and the number of warps per SM matters more than the depth of
+// each warp's load batch, so the kernels are written to stay at 64 registers or
+// fewer (4 CTAs of 256 threads per SM).  Within that budget SpMM's block path
+// keeps 8 gathers in flight per lane group (-1% to -6% against 4) and the residue
+// path, with its per-element group checks, 4.  The residue and block paths are
+// separate code regions so their registers do not add up.
 #include "ps_common.cuh"
 #include "ps_matrix.h"
 #include "ps_ops.h"
@@ -34,9 +36,10 @@ namespace {
 
 constexpr int kWarpsPerBlock = 8;
 constexpr int kThreads = kWarpsPerBlock * 32;
-constexpr int kChunk = 32;   // staged elements per lane group
-constexpr int kUnroll = 4;   // gathers in flight per lane group
-static_assert(kChunk % kUnroll == 0, "kUnroll must divide the staged chunk");
+constexpr int kChunk = 32;        // staged elements per lane group
+constexpr int kUnroll = 4;        // gathers in flight per lane group (residue, SDDMM)
+constexpr int kBlockUnroll = 8;   // gathers in flight per lane group (SpMM block groups)
+static_assert(kChunk % kUnroll == 0 && kChunk % kBlockUnroll == 0, "unrolls must divide the staged chunk");
 
 struct WorksetView {
   const int* col[kMaxWorksets];
@@ -230,29 +233,39 @@ __global__ void __launch_bounds__(kThreads, 4) spmm_fused(const SpmmArgs a) {
     }
     __syncwarp(gm);
 #pragma unroll 1
-    for (int j = 0; j < kChunk; j += kUnroll) {
-      float4 b[kUnroll];
+    for (int j = 0; j < kChunk; j += kBlockUnroll) {
+      float4 b[kBlockUnroll];
       if constexpr (kPairs) {
-        float vv[kUnroll];
+        float vv[kBlockUnroll];
 #pragma unroll
-        for (int u = 0; u < kUnroll; ++u) {
+        for (int u = 0; u < kBlockUnroll; ++u) {
           const int2 e = cv[j + u];
           b[u] = gather(e.x);
           vv[u] = __int_as_float(e.y);
         }
 #pragma unroll
-        for (int u = 0; u < kUnroll; ++u) fma4(acc, vv[u], b[u]);
+        for (int u = 0; u < kBlockUnroll; ++u) fma4(acc, vv[u], b[u]);
       } else {
-        const int4 c4 = *reinterpret_cast<const int4*>(sc + j);
-        const float4 v4 = *reinterpret_cast<const float4*>(sv + j);
-        b[0] = gather(c4.x);
-        b[1] = gather(c4.y);
-        b[2] = gather(c4.z);
-        b[3] = gather(c4.w);
-        fma4(acc, v4.x, b[0]);
-        fma4(acc, v4.y, b[1]);
-        fma4(acc, v4.z, b[2]);
-        fma4(acc, v4.w, b[3]);
+        const int4 c0 = *reinterpret_cast<const int4*>(sc + j);
+        const int4 c1 = *reinterpret_cast<const int4*>(sc + j + 4);
+        b[0] = gather(c0.x);
+        b[1] = gather(c0.y);
+        b[2] = gather(c0.z);
+        b[3] = gather(c0.w);
+        b[4] = gather(c1.x);
+        b[5] = gather(c1.y);
+        b[6] = gather(c1.z);
+        b[7] = gather(c1.w);
+        const float4 v0 = *reinterpret_cast<const float4*>(sv + j);
+        const float4 v1 = *reinterpret_cast<const float4*>(sv + j + 4);
+        fma4(acc, v0.x, b[0]);
+        fma4(acc, v0.y, b[1]);
+        fma4(acc, v0.z, b[2]);
+        fma4(acc, v0.w, b[3]);
+        fma4(acc, v1.x, b[4]);
+        fma4(acc, v1.y, b[5]);
+        fma4(acc, v1.z, b[6]);
+        fma4(acc, v1.w, b[7]);
       }
     }
     __syncwarp(gm);
@@ -615,7 +628,7 @@ void spmm_run(const Matrix& m, int N, const float* B, float* C, const float* val
   a.wide_acc = m.wide_acc;
   launch();
   const long long total = (long long)m.wide_rows * (N / 4);
-  const unsigned blocks = unsigned(std::min<long long>((total + 255) / 256, 148LL * 8));
+  const unsigned blocks = unsigned(std::min<long long>((total + 255) / 256, 8LL * device_sms()));
   wide_rows_fold<<<blocks, 256, 0, stream>>>(m.wide_row, m.wide_rows, N, m.wide_acc, C);
   PSB_LAUNCH_CHECK();
   if (capture == cudaStreamCaptureStatusNone) PSB_CUDA(cudaEventRecord(m.wide_ready, stream));
@@ -633,7 +646,7 @@ void spmm_values_launch(const Matrix& m, int N, const float* values, const float
 }
 
 void edge_softmax_launch(const Matrix& m, float* values, cudaStream_t stream) {
-  const unsigned blocks = unsigned(std::max<long long>(1, std::min<long long>(((long long)m.rows + 7) / 8, 148LL * 16)));
+  const unsigned blocks = unsigned(std::max<long long>(1, std::min<long long>(((long long)m.rows + 7) / 8, 16LL * device_sms())));
   edge_softmax_rows<<<blocks, 256, 0, stream>>>(m.row_ptr, m.rows, values);
   PSB_LAUNCH_CHECK();
 }
@@ -735,7 +748,7 @@ void spmm_launch_noalloc(const Matrix& m, int N, const float* B, float* C, cudaS
   PSB_LAUNCH_CHECK();
   if (m.wide_rows > 0) {
     const long long total = (long long)m.wide_rows * (N / 4);
-    const unsigned blocks = unsigned(std::min<long long>((total + 255) / 256, 148LL * 8));
+    const unsigned blocks = unsigned(std::min<long long>((total + 255) / 256, 8LL * device_sms()));
     wide_rows_fold<<<blocks, 256, 0, stream>>>(m.wide_row, m.wide_rows, N, a.wide_acc, C);
     PSB_LAUNCH_CHECK();
   }

@@ -252,7 +252,7 @@ bool radix_sort_pairs(K* keys, uint32_t* vals, K* keys_alt, uint32_t* vals_alt, 
 
 void iota_u32(uint32_t* vals, size_t n, cudaStream_t stream) {
   if (!n) return;
-  const unsigned blocks = unsigned(std::min<size_t>((n + 255) / 256, 148 * 32));
+  const unsigned blocks = unsigned(std::min<size_t>((n + 255) / 256, size_t(32) * device_sms()));
   iota_kernel<<<blocks, 256, 0, stream>>>(vals, n);
   PSB_LAUNCH_CHECK();
 }
