@@ -242,10 +242,18 @@ def main() -> None:
     peak, peak_kind = measured_peaks()
     achieved = alg_bytes / (ms_local * 1e-3) / 1e9
     scaling = "strong" if args.workload == "cfg5" else "weak"
+    traffic = profile_traffic("spmm_fused", f"{args.workload}_spmm_n{N}") if world == 1 else None
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "peak_source": peak_kind,
-                "traffic": profile_traffic("spmm_fused", f"{args.workload}_spmm_n{N}") if world == 1 else None,
-                "alg_bytes_per_launch": alg_bytes}
+                "traffic": traffic, "alg_bytes_per_launch": alg_bytes}
+    if traffic:
+        # The DRAM bytes the ncu capture measured per launch, over this run's launch time:
+        # how close the gathers run to the measured HBM peak.
+        roofline["dram_achieved"] = round(traffic / (ms_local * 1e-3) / 1e9, 1)
+        roofline["dram_frac"] = round(traffic / (ms_local * 1e-3) / 1e9 / peak, 4)
+    # Model, not roofline: every element gathers its dense row with no reuse.
+    roofline["no_reuse_gather_model_gbs"] = round(
+        (8.0 * panel.nnz + 4.0 * N * panel.nnz + 4.0 * N * panel.rows) / (ms_local * 1e-3) / 1e9, 1)
 
     # The other operators of the path on the same panel (kernel only, same timing rules):
     # SpMM at N=32 and SDDMM at N=32/128 (the reference's N choices).

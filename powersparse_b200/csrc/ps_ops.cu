@@ -87,7 +87,8 @@ struct SpmmArgs {
 // Block groups always add atomically and residue groups add atomically only when
 // their row has other groups, as in spmm_kernel_block.cu:155-161 and
 // spmm_kernel_residue.cu:68-81 of the reference.  Block groups accumulate FP32
-// per 32-element chunk and carry the running sum in FP64.
+// per 32-element chunk and carry the running sum in FP64; slices of wide rows add
+// that FP64 sum into the row's FP64 scratch instead of into C (Matrix::wide_rows).
 // With kValues the value of element e is a.values[csr_pos[e]] (values supplied per
 // call in CSR order) instead of the layout's sp_data[e].
 template <int LG, bool kValues = false>
@@ -276,11 +277,11 @@ __global__ void __launch_bounds__(kThreads, 4) spmm_fused(const SpmmArgs a) {
       if (t.slot >= 0) {
         // A slice of a wide row (one group per task): FP64 sum, folded into C
         // by wide_rows_fold after the launch.
-        double* acc = a.wide_acc + (long long)t.slot * a.ldb + colofs;
-        atomicAdd(acc, dx);
-        atomicAdd(acc + 1, dy);
-        atomicAdd(acc + 2, dz);
-        atomicAdd(acc + 3, dw);
+        double* row_sum = a.wide_acc + (long long)t.slot * a.ldb + colofs;
+        atomicAdd(row_sum, dx);
+        atomicAdd(row_sum + 1, dy);
+        atomicAdd(row_sum + 2, dz);
+        atomicAdd(row_sum + 3, dw);
       } else {
         emit4(Cl + (long long)des[g] * a.ldb, make_float4(float(dx), float(dy), float(dz), float(dw)), true);
       }
