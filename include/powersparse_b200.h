@@ -73,7 +73,9 @@ int ps_matrix_load(const char* path, ps_matrix** out);
 
 /* Accessors of utils/matrix_utils.h:30-40 (same meaning, same pointer kinds:
  * ps_matrix_group_num is a host array; the workset arrays are host arrays of
- * device pointers; residue offset / atomic flags are device arrays). */
+ * device pointers; residue offset / atomic flags are device arrays).  Host-only;
+ * a NULL matrix gives 0, or NULL for the pointer accessors (-1 from
+ * ps_matrix_workset_size and ps_matrix_device). */
 int ps_matrix_row(const ps_matrix* matrix);             /* MatrixRow()        */
 int ps_matrix_col(const ps_matrix* matrix);             /* MatrixCol()        */
 int ps_matrix_nnz(const ps_matrix* matrix);             /* MatrixNNZ()        */

@@ -89,33 +89,35 @@ int ps_matrix_load(const char* path, ps_matrix** out) {
   });
 }
 
-int ps_matrix_row(const ps_matrix* h) { return M(h).rows; }
-int ps_matrix_col(const ps_matrix* h) { return M(h).cols; }
-int ps_matrix_nnz(const ps_matrix* h) { return M(h).nnz; }
-int ps_matrix_group_type_num(const ps_matrix* h) { return M(h).S; }
-int ps_matrix_group_fine_size(const ps_matrix* h) { return M(h).fine; }
-const int* ps_matrix_group_num(const ps_matrix* h) { return M(h).group_num.data(); }
+// Accessors: host-only reads of the handle; a NULL handle gives 0 / NULL.
+int ps_matrix_row(const ps_matrix* h) { return h ? M(h).rows : 0; }
+int ps_matrix_col(const ps_matrix* h) { return h ? M(h).cols : 0; }
+int ps_matrix_nnz(const ps_matrix* h) { return h ? M(h).nnz : 0; }
+int ps_matrix_group_type_num(const ps_matrix* h) { return h ? M(h).S : 0; }
+int ps_matrix_group_fine_size(const ps_matrix* h) { return h ? M(h).fine : 0; }
+const int* ps_matrix_group_num(const ps_matrix* h) { return h ? M(h).group_num.data() : nullptr; }
 const int* const* ps_matrix_workset_col_ind(const ps_matrix* h) {
-  return const_cast<const int* const*>(M(h).col_ind.data());
+  return h ? const_cast<const int* const*>(M(h).col_ind.data()) : nullptr;
 }
 const float* const* ps_matrix_workset_sp_data(const ps_matrix* h) {
-  return const_cast<const float* const*>(M(h).sp_data.data());
+  return h ? const_cast<const float* const*>(M(h).sp_data.data()) : nullptr;
 }
 const int* const* ps_matrix_group_destination(const ps_matrix* h) {
-  return const_cast<const int* const*>(M(h).group_des.data());
+  return h ? const_cast<const int* const*>(M(h).group_des.data()) : nullptr;
 }
 const int* const* ps_matrix_csr_position(const ps_matrix* h) {
-  return const_cast<const int* const*>(M(h).csr_pos.data());
+  return h ? const_cast<const int* const*>(M(h).csr_pos.data()) : nullptr;
 }
-const int* ps_matrix_residue_offset(const ps_matrix* h) { return M(h).residue_offset; }
-const bool* ps_matrix_residue_atomic(const ps_matrix* h) { return M(h).residue_atomic; }
+const int* ps_matrix_residue_offset(const ps_matrix* h) { return h ? M(h).residue_offset : nullptr; }
+const bool* ps_matrix_residue_atomic(const ps_matrix* h) { return h ? M(h).residue_atomic : nullptr; }
 long long ps_matrix_workset_size(const ps_matrix* h, int s) {
+  if (!h) return -1;
   const psb::Matrix& m = M(h);
   return (s < 0 || s >= m.S) ? -1 : m.ws_size[s];
 }
-double ps_matrix_preprocess_ms(const ps_matrix* h) { return M(h).preprocess_ms; }
-int ps_matrix_device(const ps_matrix* h) { return M(h).device; }
-int ps_matrix_wide_rows(const ps_matrix* h) { return M(h).wide_rows; }
+double ps_matrix_preprocess_ms(const ps_matrix* h) { return h ? M(h).preprocess_ms : 0.0; }
+int ps_matrix_device(const ps_matrix* h) { return h ? M(h).device : -1; }
+int ps_matrix_wide_rows(const ps_matrix* h) { return h ? M(h).wide_rows : 0; }
 
 int ps_spmm(const ps_matrix* h, int N, const float* B, float* C, void* stream) {
   return guarded([&] {

@@ -91,3 +91,18 @@ def test_partition_rows_more_parts_than_rows():
 
 def test_group_size_macro():
     assert [psb.GROUP_SIZE(s) for s in range(1, 6)] == [32, 64, 128, 256, 512]
+
+
+def test_accessors_of_a_null_matrix_do_not_dereference_it():
+    """Host-only accessors return 0 / NULL (-1 where -1 already means "invalid")."""
+    lib = psb.load_library()
+    for name in ("ps_matrix_row", "ps_matrix_col", "ps_matrix_nnz", "ps_matrix_group_type_num",
+                 "ps_matrix_group_fine_size", "ps_matrix_wide_rows"):
+        assert getattr(lib, name)(None) == 0, name
+    for name in ("ps_matrix_group_num", "ps_matrix_workset_col_ind", "ps_matrix_workset_sp_data",
+                 "ps_matrix_group_destination", "ps_matrix_csr_position", "ps_matrix_residue_offset",
+                 "ps_matrix_residue_atomic"):
+        assert not getattr(lib, name)(None), name
+    assert lib.ps_matrix_workset_size(None, 0) == -1
+    assert lib.ps_matrix_device(None) == -1
+    assert lib.ps_matrix_preprocess_ms(None) == 0.0
