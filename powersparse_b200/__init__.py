@@ -9,6 +9,17 @@ operator API for Python callers and tests:
     SpMM(matrix, N, B, C, stream=None)             (PowerSparse_SpMM/PowerSparse_SpMM.h:14-17)
     SDDMM(matrix, N, lhs, rhs, outputs, stream=None) (PowerSparse_SDDMM/PowerSparse_SDDMM.h:14-18)
 
+and the additions after the path (no reference counterpart):
+
+    SDDMM_csr(matrix, N, lhs, rhs, out)        SDDMM written in the input's CSR order
+    edge_softmax_csr(matrix, values)           per-row softmax of CSR-order edge values
+    SpMM_values(matrix, N, values, B, C)       SpMM with per-call CSR-order edge values
+    PowerSparseMatrixGPU.save(path) / .load(path)   layout cache
+    partition_rows(row_ptr, parts)             nnz-balanced row panels (multi-GPU)
+
+``powersparse_b200.torch_ops`` registers the operators as ``torch.ops.powersparse.*``
+and ``powersparse_b200.distributed`` shards them by row panels over torch.distributed.
+
 Errors raise ``ValueError`` where the reference throws std::invalid_argument and
 ``RuntimeError`` where it throws std::runtime_error.  Dense operands are CUDA
 torch tensors (or raw device addresses as ints); every computation runs in the
