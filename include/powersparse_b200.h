@@ -116,7 +116,15 @@ int ps_matrix_wide_rows(const ps_matrix* matrix);
  * the kernel launches of PowerSparse::SpMM (PowerSparse_SpMM/PowerSparse_SpMM.h:14-17,
  * PowerSparse_SpMM/spmm_solution.cu:7-34) with one fused launch.  Dense offsets
  * are 64-bit, so the reference's rows*N, cols*N <= INT_MAX limit
- * (utils/matrix_utils.h:72-76) does not apply. */
+ * (utils/matrix_utils.h:72-76) does not apply.
+ * Stream capture: on a matrix with wide rows (ps_matrix_wide_rows > 0) the call
+ * uses an FP64 scratch kept in the matrix, allocated by the first call at a
+ * larger N than before; that first call cannot be captured (PS_ERR_CUDA), so
+ * call once eagerly at each N before capturing.  Eager calls on one matrix are
+ * ordered on the device by the library; replays of a captured call are not:
+ * order them against other calls on the same matrix (one stream, or events).
+ * A scratch buffer replaced by a larger one stays allocated until
+ * ps_matrix_destroy, so earlier captures stay valid. */
 int ps_spmm(const ps_matrix* matrix, int N, const float* B, float* C, void* stream);
 
 /* ps_spmm that allocates no device memory.  No counterpart in the reference.
@@ -128,10 +136,13 @@ int ps_spmm(const ps_matrix* matrix, int N, const float* B, float* C, void* stre
  * fixed 16 MiB device array instead (2^21 doubles, held by every GPU that
  * loads the library until exit) and fails with PS_ERR_INVALID_ARGUMENT when
  * ps_matrix_wide_rows(matrix) * N exceeds 2^21.  Same inputs, outputs and
- * results as ps_spmm.  The first call on a device resolves the array's device
- * address; make that first call before any stream capture.  All calls share
- * the array: calls that overlap on the GPU (other streams, other matrices)
- * race and give wrong results. */
+ * results as ps_spmm.  The array's device address is resolved when a matrix is
+ * created or loaded on a device (ps_matrix_create / ps_matrix_load): that is
+ * where the library's operator code, the array among it, is loaded onto the
+ * device and allocated, so the calls themselves allocate nothing.  All calls
+ * share the array and it keeps what the last call left in it (each call clears
+ * the part it uses): calls that overlap on the GPU (other streams, other
+ * matrices) race and give wrong results. */
 int ps_spmm_noalloc(const ps_matrix* matrix, int N, const float* B, float* C, void* stream);
 
 /* FP32 SDDMM on `stream`, asynchronous: for every element e of workset s,

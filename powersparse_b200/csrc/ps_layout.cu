@@ -18,6 +18,7 @@
 // sort over exactly the bits in use; the resulting orders are identical.
 #include "ps_common.cuh"
 #include "ps_matrix.h"
+#include "ps_ops.h"
 #include "ps_sort.cuh"
 
 #include <algorithm>
@@ -43,6 +44,7 @@ Matrix::~Matrix() {
   cudaFree(row_ptr);
   cudaFree(wide_row);
   cudaFree(wide_acc);
+  for (auto p : wide_acc_retired) cudaFree(p);
   if (wide_ready) cudaEventDestroy(wide_ready);
 }
 
@@ -345,8 +347,10 @@ void validate_csr(int rows, int cols, int nnz, const int* row_ptr, const int* co
 // N = 32), the same order concentrates the requests of every SM on a few lines at
 // once and row order is 6% faster.
 // `slot_of[s][g]`: wide-row slot of block group g of workset s (empty: none).
-std::vector<Task> build_block_tasks(const Matrix& m, BlockOrder order, const std::vector<std::vector<int>>& slot_of) {
+std::vector<Task> build_block_tasks(const Matrix& m, BlockOrder order, const std::vector<std::vector<int>>& slot_of,
+                                    const std::vector<char>& exact_slot) {
   auto slot = [&](int s, int g) { return slot_of[s].empty() ? -1 : slot_of[s][g]; };
+  auto exact = [&](int s, int g) { const int k = slot(s, g); return k >= 0 && exact_slot[size_t(k)] ? 1 : 0; };
   std::vector<Task> tasks;
   for (int s = m.S - 1; s >= 1; --s) {
     const int G = group_size(s);
@@ -354,16 +358,16 @@ std::vector<Task> build_block_tasks(const Matrix& m, BlockOrder order, const std
     if (G >= kTaskElems && order == kRowOrder) {
       for (int g = 0; g < groups; ++g)
         for (int off = 0; off < G; off += kTaskElems)
-          tasks.push_back({s, g * G + off, g * G + std::min(G, off + kTaskElems), g, slot(s, g)});
+          tasks.push_back({s, g * G + off, g * G + std::min(G, off + kTaskElems), g, slot(s, g), exact(s, g)});
     } else if (G >= kTaskElems) {
       for (int off = 0; off < G; off += kTaskElems)
         for (int g = 0; g < groups; ++g)
-          tasks.push_back({s, g * G + off, g * G + std::min(G, off + kTaskElems), g, slot(s, g)});
+          tasks.push_back({s, g * G + off, g * G + std::min(G, off + kTaskElems), g, slot(s, g), exact(s, g)});
     } else {
       const int per = kTaskElems / G;
       for (int g = 0; g < groups; g += per) {
         const int ge = std::min(groups, g + per);
-        tasks.push_back({s, g * G, ge * G, g, -1});
+        tasks.push_back({s, g * G, ge * G, g, -1, 0});
       }
     }
   }
@@ -382,7 +386,7 @@ std::vector<Task> build_residue_tasks(const Matrix& m, const std::vector<int>& h
     const int begin = h_res_off[g];
     while (g < G0 && h_res_off[g + 1] - begin <= elems) ++g;
     if (g == first) ++g;  // a single group longer than a task (cannot happen: <= 31 or 16)
-    tasks.push_back({0, begin, h_res_off[g], first, -1});
+    tasks.push_back({0, begin, h_res_off[g], first, -1, 0});
   }
   return tasks;
 }
@@ -418,6 +422,7 @@ void finish_matrix(Matrix& mat, const std::vector<int>& h_res_off) {
   // Wide rows (kWideRowSlices): block slices per row, counted over the groups of
   // the worksets whose groups are cut into slices; slots in row order.
   std::vector<std::vector<int>> slot_of(S);
+  std::vector<char> exact_slot;  // per wide-row slot: exact FP64 products
   {
     std::vector<std::vector<int>> h_des(S);
     std::vector<int> slices(size_t(m->rows), 0);
@@ -433,6 +438,7 @@ void finish_matrix(Matrix& mat, const std::vector<int>& h_res_off) {
       if (slices[r] >= kWideRowSlices) {
         slot_of_row[r] = int(h_wide_row.size());
         h_wide_row.push_back(r);
+        exact_slot.push_back(slices[r] >= kExactRowSlices ? 1 : 0);
       }
     }
     m->wide_rows = int(h_wide_row.size());
@@ -454,7 +460,8 @@ void finish_matrix(Matrix& mat, const std::vector<int>& h_res_off) {
     PSB_CUDA(cudaMemcpy(*dst, tasks.data(), sizeof(Task) * tasks.size(), cudaMemcpyHostToDevice));
   };
   for (int o : {kRowOrder, kSliceOrder})
-    upload_tasks(build_block_tasks(*m, BlockOrder(o), slot_of), &m->block_tasks[o], &m->num_block_tasks[o]);
+    upload_tasks(build_block_tasks(*m, BlockOrder(o), slot_of, exact_slot), &m->block_tasks[o],
+                 &m->num_block_tasks[o]);
   upload_tasks(build_residue_tasks(*m, h_res_off, kFineResidueTaskElems), &m->residue_tasks[kFineResidue],
                &m->num_residue_tasks[kFineResidue]);
   upload_tasks(build_residue_tasks(*m, h_res_off, kTaskElems), &m->residue_tasks[kCoarseResidue],
@@ -462,6 +469,7 @@ void finish_matrix(Matrix& mat, const std::vector<int>& h_res_off) {
   int l2 = 0;
   PSB_CUDA(cudaDeviceGetAttribute(&l2, cudaDevAttrL2CacheSize, m->device));
   m->l2_bytes = l2;
+  noalloc_prepare(m->device);
   PSB_CUDA(cudaDeviceSynchronize());
 }
 

@@ -19,13 +19,16 @@ inline int group_size(int s) { return 32 << (s - 1); }
 // A unit of SpMM/SDDMM work: elements [begin, end) of workset `ws`, starting in
 // group `group`.  Residue tasks cover whole groups; block tasks cover whole
 // groups, or one slice of a group when the group is longer than a task.
-// `slot` >= 0 marks a slice of a wide row (see Matrix::wide_rows).
+// `slot` >= 0 marks a slice of a wide row (see Matrix::wide_rows); `exact` marks
+// the slices of the longest wide rows (kExactRowSlices), which sum exact FP64
+// products.
 struct Task {
   int ws;
   int begin;
   int end;
   int group;
   int slot;
+  int exact;
 };
 
 // A launch runs the block tasks (largest groups first), then the residue tasks.
@@ -78,9 +81,12 @@ struct Matrix {
   int wide_rows = 0;
   int* wide_row = nullptr;             // device [wide_rows]: row of each slot
   // FP64 scratch of the wide rows, grown on demand to wide_rows * N doubles and
-  // all-zero between calls.  Calls that use it are ordered by `wide_ready`.
+  // all-zero between calls.  Eager calls that use it are ordered by `wide_ready`.
+  // Buffers replaced by a larger one stay allocated until the matrix is destroyed
+  // (a captured CUDA graph may still use them).
   mutable double* wide_acc = nullptr;
   mutable long long wide_acc_cap = 0;  // doubles
+  mutable std::vector<double*> wide_acc_retired;
   mutable cudaEvent_t wide_ready = nullptr;
   mutable std::mutex wide_mutex;
 
@@ -119,5 +125,12 @@ constexpr int kFineResidueTaskElems = 64;
 // k >= 8 (rows of >= 2048 elements, R ~ sqrt(row length)) reaches 1e-5, the
 // absolute tolerance, on outputs whose exact value is near zero.
 constexpr int kWideRowSlices = 8;
+// Wide rows with at least this many block slices (65536 elements) add exact FP64
+// products; shorter wide rows add products in Kahan-compensated FP32.  The FMA
+// rounds each product's addend once (about 2^-24 * |v * b|), and over L products
+// those roundings drift by about sqrt(L) * 2^-24 * 0.2 for values in [0, 1] times
+// operands in [-1, 1]: 1e-6 at 65536 elements, 5e-6 at 667k (the longest row of
+// configuration 5), against the 1e-5 absolute tolerance.
+constexpr int kExactRowSlices = 256;
 
 }  // namespace psb

@@ -56,6 +56,15 @@ __device__ __forceinline__ void fma4(float4& acc, float s, const float4& b) {
   acc.w = fmaf(s, b.w, acc.w);
 }
 
+// Kahan step: s + c tracks sum(v * b) with the rounding error of every add kept in
+// c (the product enters exactly through the FMA).
+__device__ __forceinline__ void kahan(float& s, float& c, float v, float b) {
+  const float y = fmaf(v, b, -c);
+  const float t = s + y;
+  c = (t - s) - y;
+  s = t;
+}
+
 __device__ __forceinline__ float dot4(const float4& a, const float4& b) {
   return fmaf(a.w, b.w, fmaf(a.z, b.z, fmaf(a.y, b.y, a.x * b.x)));
 }
@@ -233,45 +242,82 @@ __global__ void __launch_bounds__(kThreads, 4) spmm_fused(const SpmmArgs a) {
       *reinterpret_cast<float4*>(sv + 4 * (l - 8)) = value4(base, l - 8);
     }
     __syncwarp(gm);
-#pragma unroll 1
-    for (int j = 0; j < kChunk; j += kBlockUnroll) {
-      float4 b[kBlockUnroll];
+    // The gathers and values of elements j .. j + 3 of the chunk.
+    auto load4 = [&](int j, float4* b, float* vv) {
       if constexpr (kPairs) {
-        float vv[kBlockUnroll];
 #pragma unroll
-        for (int u = 0; u < kBlockUnroll; ++u) {
+        for (int u = 0; u < 4; ++u) {
           const int2 e = cv[j + u];
           b[u] = gather(e.x);
           vv[u] = __int_as_float(e.y);
         }
-#pragma unroll
-        for (int u = 0; u < kBlockUnroll; ++u) fma4(acc, vv[u], b[u]);
       } else {
         const int4 c0 = *reinterpret_cast<const int4*>(sc + j);
-        const int4 c1 = *reinterpret_cast<const int4*>(sc + j + 4);
         b[0] = gather(c0.x);
         b[1] = gather(c0.y);
         b[2] = gather(c0.z);
         b[3] = gather(c0.w);
-        b[4] = gather(c1.x);
-        b[5] = gather(c1.y);
-        b[6] = gather(c1.z);
-        b[7] = gather(c1.w);
         const float4 v0 = *reinterpret_cast<const float4*>(sv + j);
-        const float4 v1 = *reinterpret_cast<const float4*>(sv + j + 4);
-        fma4(acc, v0.x, b[0]);
-        fma4(acc, v0.y, b[1]);
-        fma4(acc, v0.z, b[2]);
-        fma4(acc, v0.w, b[3]);
-        fma4(acc, v1.x, b[4]);
-        fma4(acc, v1.y, b[5]);
-        fma4(acc, v1.z, b[6]);
-        fma4(acc, v1.w, b[7]);
+        vv[0] = v0.x; vv[1] = v0.y; vv[2] = v0.z; vv[3] = v0.w;
       }
+    };
+    if (t.slot >= 0 && t.exact) {
+      // Slices of the longest wide rows (Task::exact) add exact products (an FP32 x
+      // FP32 product is exact in FP64) in FP64.  Four gathers at a time: the FP64
+      // sums hold the registers of the other four.
+#pragma unroll 1
+      for (int j = 0; j < kChunk; j += 4) {
+        float4 b[4];
+        float vv[4];
+        load4(j, b, vv);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const double v = vv[u];
+          dx = fma(v, double(b[u].x), dx);
+          dy = fma(v, double(b[u].y), dy);
+          dz = fma(v, double(b[u].z), dz);
+          dw = fma(v, double(b[u].w), dw);
+        }
+      }
+    } else if (t.slot >= 0) {
+      // Other wide-row slices: Kahan-compensated FP32 over the chunk, the sum and its
+      // compensation folded into FP64 separately.  Plain FP32 chunk sums would drift
+      // by about sqrt(chunks) * 2^-24 * |chunk sum| over rows of thousands of
+      // elements, above the 1e-5 absolute tolerance where the exact value is near
+      // zero; rows that are not wide hold at most ~2300 elements and keep them.
+      float4 ks = make_float4(0.f, 0.f, 0.f, 0.f), kc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 1
+      for (int j = 0; j < kChunk; j += kBlockUnroll) {
+        float4 b[kBlockUnroll];
+        float vv[kBlockUnroll];
+        load4(j, b, vv);
+        load4(j + 4, b + 4, vv + 4);
+#pragma unroll
+        for (int u = 0; u < kBlockUnroll; ++u) {
+          kahan(ks.x, kc.x, vv[u], b[u].x);
+          kahan(ks.y, kc.y, vv[u], b[u].y);
+          kahan(ks.z, kc.z, vv[u], b[u].z);
+          kahan(ks.w, kc.w, vv[u], b[u].w);
+        }
+      }
+      dx += double(ks.x) - double(kc.x);
+      dy += double(ks.y) - double(kc.y);
+      dz += double(ks.z) - double(kc.z);
+      dw += double(ks.w) - double(kc.w);
+    } else {
+      float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);  // FP32 sum of this chunk
+#pragma unroll 1
+      for (int j = 0; j < kChunk; j += kBlockUnroll) {
+        float4 b[kBlockUnroll];
+        float vv[kBlockUnroll];
+        load4(j, b, vv);
+        load4(j + 4, b + 4, vv + 4);
+#pragma unroll
+        for (int u = 0; u < kBlockUnroll; ++u) fma4(sum, vv[u], b[u]);
+      }
+      dx += sum.x; dy += sum.y; dz += sum.z; dw += sum.w;
     }
     __syncwarp(gm);
-    dx += acc.x; dy += acc.y; dz += acc.z; dw += acc.w;
-    acc = make_float4(0.f, 0.f, 0.f, 0.f);
     const int next = base + kChunk;
     if (next == t.end || next % G == 0) {
       if (t.slot >= 0) {
@@ -607,9 +653,12 @@ void spmm_run(const Matrix& m, int N, const float* B, float* C, const float* val
     launch();
     return;
   }
-  // Wide rows: the matrix's FP64 scratch.  Calls that share it are serialized on
-  // the device through wide_ready (the scratch is all-zero again when a call's
-  // fold kernel ends); a larger N grows it once, after the last user finished.
+  // Wide rows: the matrix's FP64 scratch.  Eager calls that share it are
+  // serialized on the device through wide_ready (the scratch is all-zero again
+  // when a call's fold kernel ends).  A larger N grows it: the smaller buffer is
+  // retired, not freed, because a CUDA graph captured earlier may still hold it;
+  // retired buffers are freed with the matrix.  Captured calls skip the event
+  // (replays are ordered by the caller, as documented for ps_spmm).
   std::lock_guard<std::mutex> lock(m.wide_mutex);
   const long long need = (long long)m.wide_rows * N;
   cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
@@ -617,8 +666,7 @@ void spmm_run(const Matrix& m, int N, const float* B, float* C, const float* val
   if (m.wide_acc_cap < need) {
     if (capture != cudaStreamCaptureStatusNone)
       throw std::runtime_error("SpMM at a new N cannot be captured: call it once with this N before capturing");
-    PSB_CUDA(cudaEventSynchronize(m.wide_ready));
-    PSB_CUDA(cudaFree(m.wide_acc));
+    if (m.wide_acc) m.wide_acc_retired.push_back(m.wide_acc);
     m.wide_acc = nullptr;
     m.wide_acc_cap = 0;
     PSB_CUDA(cudaMalloc(reinterpret_cast<void**>(&m.wide_acc), sizeof(double) * size_t(need)));
@@ -717,6 +765,18 @@ double* noalloc_scratch(int device) {
 }
 
 }  // namespace
+
+void noalloc_prepare(int device) {
+  noalloc_scratch(device);
+  // With lazy loading (the CUDA 12 default) a kernel's code is loaded onto the
+  // device at its first use; querying its attributes loads it now, so the first
+  // ps_spmm_noalloc call on a device does not.
+  cudaFuncAttributes attr;
+  PSB_CUDA(cudaFuncGetAttributes(&attr, spmm_fused<8>));
+  PSB_CUDA(cudaFuncGetAttributes(&attr, spmm_fused<16>));
+  PSB_CUDA(cudaFuncGetAttributes(&attr, spmm_fused<32>));
+  PSB_CUDA(cudaFuncGetAttributes(&attr, wide_rows_fold));
+}
 
 void spmm_launch_noalloc(const Matrix& m, int N, const float* B, float* C, cudaStream_t stream) {
   const long long need = (long long)m.wide_rows * N;

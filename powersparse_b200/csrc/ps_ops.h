@@ -25,6 +25,11 @@ void edge_softmax_launch(const Matrix& m, float* values, cudaStream_t stream);
 // GPU share the array and race.
 constexpr long long kNoAllocScratchDoubles = 1LL << 21;  // 16 MiB
 void spmm_launch_noalloc(const Matrix& m, int N, const float* B, float* C, cudaStream_t stream);
+// Resolves the fixed array's address on `device` (the current device).  The first
+// resolution loads this library's operator code onto the device, which allocates
+// (the array among it); matrices call this when they are created or loaded, so
+// spmm_launch_noalloc itself never does.
+void noalloc_prepare(int device);
 
 // out[s][e] (+)= A_e * <lhs[row(e)], rhs[col(e)]>; N is 32 or 128.
 void sddmm_launch(const Matrix& m, int N, const float* lhs, const float* rhs, float* const* out,

@@ -53,10 +53,34 @@ def chung_lu_pairs(n: int, mean: float, dmax: float, gamma: float, seed: int, ov
     gen.manual_seed(seed)
     w = _weights(n, mean, dmax, gamma, device)
     perm = torch.randperm(n, generator=gen, device=device)
-    w = w[perm]
+    return _pairs_by_weight(w[perm], int(round(n * mean / 2 * oversample)), gen)
+
+
+def lognormal_pairs(n: int, mean: float, sigma: float, cap: float, seed: int, oversample: float,
+                    device="cuda") -> torch.Tensor:
+    """Unique undirected pairs of a Chung-Lu graph with lognormal expected degrees
+    capped at ``cap`` (the model of ``synth.lognormal_graph``)."""
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed)
+    z = torch.randn(n, generator=gen, device=device, dtype=torch.float64)
+    lo, hi = -10.0, 20.0
+    for _ in range(80):
+        mu = 0.5 * (lo + hi)
+        if torch.clamp(torch.exp(mu + sigma * z), max=cap).mean().item() > mean:
+            hi = mu
+        else:
+            lo = mu
+    w = torch.clamp(torch.exp(mu + sigma * z), min=1.0, max=cap)
+    return _pairs_by_weight(w, int(round(n * mean / 2 * oversample)), gen)
+
+
+def _pairs_by_weight(w: torch.Tensor, m: int, gen: torch.Generator) -> torch.Tensor:
+    """``m`` endpoint pairs drawn with probability proportional to ``w`` (self loops
+    dropped), as unique sorted keys a*n+b with a < b."""
+    n = w.numel()
+    device = w.device
     cdf = torch.cumsum(w, 0)
     cdf /= cdf[-1].clone()
-    m = int(round(n * mean / 2 * oversample))
     keys = []
     chunk = 1 << 26
     for s in range(0, m, chunk):
@@ -139,6 +163,28 @@ def config5_pairs(device="cuda"):
     """Configuration 5: R-MAT scale 24, edge factor 64, (a,b,c,d) = (.57,.19,.19,.05)."""
     p = synth.CONFIGS[5]
     return rmat_pairs(p["scale"], p["edge_factor"], seed=5, device=device)
+
+
+def config_pairs(cfg: int, device="cuda"):
+    """(nodes, unique pairs) of benchmark configuration 2, 3, 4 or 5 at full size
+    (graph seed = configuration number; the GPU sampler, not synth.config_matrix's
+    numpy stream, so the graphs differ from the CPU generator's but share its law)."""
+    if cfg == 5:
+        return config5_pairs(device=device)
+    p = synth.CONFIGS[cfg]
+    if p["kind"] == "chung_lu":
+        return p["n"], chung_lu_pairs(p["n"], p["mean"], p["dmax"], p["gamma"], seed=cfg,
+                                      oversample=p["oversample"], device=device)
+    if p["kind"] == "lognormal":
+        return p["n"], lognormal_pairs(p["n"], p["mean"], p["sigma"], p["cap"], seed=cfg,
+                                       oversample=p["oversample"], device=device)
+    raise ValueError(f"configuration {cfg} has no GPU generator")
+
+
+def config_matrix(cfg: int, device="cuda") -> synth.Csr:
+    """The whole matrix of configuration ``cfg`` (2-5) as a host CSR, generated on the GPU."""
+    n, pairs = config_pairs(cfg, device=device)
+    return panel_from_pairs(pairs, n, 0, n, seed=cfg, values=synth.CONFIGS[cfg]["values"])
 
 
 def config2_pairs(nodes_scale: int = 1, device="cuda"):

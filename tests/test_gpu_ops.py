@@ -262,3 +262,72 @@ def test_spmm_large_n_uses_several_slabs():
         for n in (160, 384, 1024):
             B = dense_inputs(mtx.cols, n, n)
             _assert_close(_spmm(m, B).cpu().numpy(), oracle.spmm(mtx.row_ptr, mtx.col_ind, mtx.values, B), f"N={n}")
+
+
+def test_spmm_graph_capture_keeps_its_scratch_when_a_larger_n_grows_it():
+    """A CUDA graph captured around SpMM on a matrix with wide rows holds the matrix's
+    FP64 scratch of that N.  A later eager call at a larger N allocates a larger
+    scratch; the captured one stays allocated (retired, freed with the matrix), so
+    replays of the graph still give the oracle's result.  Capturing the first call at
+    a new N is refused (it would allocate inside the capture)."""
+    mtx = _heavy_rows_matrix(23)
+    with psb.PowerSparseMatrixGPU(mtx.rows, mtx.cols, mtx.nnz, mtx.row_ptr, mtx.col_ind, mtx.values,
+                                  sm_count=1) as m:
+        assert m.wide_rows > 0
+        B32 = synth.dense(mtx.cols, 32, 71)
+        exp32 = oracle.spmm(mtx.row_ptr, mtx.col_ind, mtx.values, B32)
+        dB32 = torch.from_numpy(B32).cuda()
+        C32 = torch.zeros((mtx.rows, 32), device="cuda")
+        psb.SpMM(m, 32, dB32, C32)  # eager call at N=32 sizes the scratch
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            C32.zero_()
+            psb.SpMM(m, 32, dB32, C32, torch.cuda.current_stream())
+        B128 = synth.dense(mtx.cols, 128, 72)
+        C128 = torch.zeros((mtx.rows, 128), device="cuda")
+        psb.SpMM(m, 128, torch.from_numpy(B128).cuda(), C128)  # grows the scratch
+        torch.cuda.synchronize()
+        _assert_close(C128.cpu().numpy(), oracle.spmm(mtx.row_ptr, mtx.col_ind, mtx.values, B128), "eager N=128")
+        for replay in range(2):
+            C32.fill_(7.0)
+            g.replay()
+            torch.cuda.synchronize()
+            _assert_close(C32.cpu().numpy(), exp32, f"replay {replay}")
+        del g
+        C256 = torch.zeros((mtx.rows, 256), device="cuda")
+        B256 = torch.zeros((mtx.cols, 256), device="cuda")
+        g2 = torch.cuda.CUDAGraph()
+        with pytest.raises(RuntimeError, match="cannot be captured"):
+            with torch.cuda.graph(g2):
+                psb.SpMM(m, 256, B256, C256, torch.cuda.current_stream())
+        torch.cuda.synchronize()
+
+
+def test_spmm_rows_longer_than_65536_use_exact_products():
+    """Two rows of ~70k and ~120k nonzeros (at least 256 block slices: the exact FP64
+    product path) next to light rows and a wide row of ~3k (the compensated FP32 path):
+    every output within tolerance of the FP64 oracle, at N = 32 and 128."""
+    base = synth.chung_lu(3000, 12, 300, 2.1, seed=24)
+    rng = np.random.default_rng(24)
+    cols = 200_000
+    ptr, col, val = [0], [], []
+    for r in range(base.rows):
+        lo, hi = base.row_ptr[r], base.row_ptr[r + 1]
+        c, v = list(base.col_ind[lo:hi]), list(base.values[lo:hi])
+        k = {5: 70_000, 1500: 120_000, 2500: 3_000}.get(r, 0)
+        if k:
+            c = np.sort(rng.choice(cols, size=k, replace=False)).tolist()
+            v = rng.uniform(0, 1, size=k).astype(np.float32).tolist()
+        col += c
+        val += v
+        ptr.append(len(col))
+    mtx = synth.Csr(base.rows, cols, np.array(ptr, np.int32), np.array(col, np.int32), np.array(val, np.float32),
+                    False)
+    with psb.PowerSparseMatrixGPU(mtx.rows, mtx.cols, mtx.nnz, mtx.row_ptr, mtx.col_ind, mtx.values,
+                                  sm_count=1) as m:
+        assert m.wide_rows >= 3
+        for n in (32, 128):
+            B = synth.dense(mtx.cols, n, 80 + n)
+            _assert_close(_spmm(m, B).cpu().numpy(), oracle.spmm(mtx.row_ptr, mtx.col_ind, mtx.values, B),
+                          f"N={n}")
