@@ -5,9 +5,11 @@ the GPU's memory up front and hand it out from their own pool, and latency-bound
 callers that cannot take the synchronization cudaMalloc / cudaFree may imply.
 For them ps_spmm_noalloc keeps the FP64 wide-row scratch of SpMM in a fixed
 16 MiB device array instead of a buffer grown with cudaMalloc.  This file checks,
-through the C ABI, that two calls in a row give ps_spmm's results within the
-tolerance of the other GPU tests, and that a matrix needing more scratch than the
-array holds is refused with a clear error.  It is named to be collected last.
+through the C ABI, that two calls in a row give the FP64 oracle's results (and
+ps_spmm's) within the tolerance of the other GPU tests, that the device's free
+memory is the same before and after those calls on a fresh matrix at an N that
+ps_spmm never ran, and that a matrix needing more scratch than the array holds is
+refused with a clear error.  It is named to be collected last.
 """
 import ctypes
 
@@ -47,24 +49,31 @@ def _check(actual, expected, tag):
     assert ok.all(), f"{tag}: {int((~ok).sum())} of {ok.size} outside tolerance"
 
 
-@pytest.mark.parametrize("n", [32, 128, 256])
-def test_noalloc_spmm_matches_spmm_on_two_calls(n):
+@pytest.mark.parametrize("n", [32, 96, 128, 256])
+def test_noalloc_spmm_matches_oracle_and_spmm_on_two_calls(n):
     mtx = synth.chung_lu(3000, 14, 600, 2.1, seed=31)
     wide = _wide_matrix(64, 4096, 2048, 32)
     for A, sm in ((mtx, 1), (wide, 1)):
         with psb.PowerSparseMatrixGPU(A.rows, A.cols, A.nnz, A.row_ptr, A.col_ind, A.values, sm_count=sm) as m:
             if A is wide:
                 assert m.wide_rows == A.rows
-            B = torch.from_numpy(synth.dense(A.cols, n, 50 + n)).cuda()
+            B_host = synth.dense(A.cols, n, 50 + n)
+            B = torch.from_numpy(B_host).cuda()
+            outs = [torch.zeros((A.rows, n), device="cuda") for _ in range(2)]
+            torch.cuda.synchronize()
+            free_before = torch.cuda.mem_get_info()[0]
+            for C in outs:  # two calls in a row; this N never ran through ps_spmm on this matrix
+                status, err = _noalloc(m, n, B, C)
+                assert status == psb.PS_OK, err
+            torch.cuda.synchronize()
+            assert torch.cuda.mem_get_info()[0] == free_before, "device memory was allocated"
+            expected = oracle.spmm(A.row_ptr, A.col_ind, A.values, B_host)
+            for call, C in enumerate(outs):
+                _check(C.cpu().numpy(), expected, f"N={n} call {call} vs the FP64 oracle")
             C_ref = torch.zeros((A.rows, n), device="cuda")
             psb.SpMM(m, n, B, C_ref)
             torch.cuda.synchronize()
-            for call in range(2):
-                C = torch.zeros((A.rows, n), device="cuda")
-                status, err = _noalloc(m, n, B, C)
-                torch.cuda.synchronize()
-                assert status == psb.PS_OK, err
-                _check(C.cpu().numpy(), C_ref.cpu().numpy().astype(np.float64), f"N={n} call {call}")
+            _check(outs[1].cpu().numpy(), C_ref.cpu().numpy().astype(np.float64), f"N={n} vs ps_spmm")
 
 
 def test_noalloc_spmm_refuses_more_scratch_than_the_array_holds():
