@@ -8,6 +8,7 @@ Outputs (git-ignored, shipped with the tree):
   powersparse_b200/lib/libpowersparse.so       the reference's C++ operator API over the C ABI
   powersparse_b200/bin/powersparse_spmm        drop-in benchmark CLI (SpMM)
   powersparse_b200/bin/powersparse_sddmm       drop-in benchmark CLI (SDDMM)
+  powersparse_b200/bin/powersparse_mtx2csr     MatrixMarket -> binary CSR converter
 """
 from __future__ import annotations
 
@@ -62,7 +63,9 @@ def build_cuda(force: bool = False) -> str:
 def build_cxx(force: bool = False) -> None:
     """The reference's C++ API (namespace PowerSparse) and the drop-in CLI."""
     host = sorted(glob.glob(os.path.join(CSRC, "host", "*.cpp")))
-    cli = sorted(glob.glob(os.path.join(CSRC, "cli", "*.cpp")))
+    reader = [os.path.join(CSRC, "cli", "matrix_market.cpp")]
+    cli = [os.path.join(CSRC, "cli", "benchmark.cpp")] + reader
+    convert = [os.path.join(CSRC, "cli", "mtx2csr.cpp")] + reader
     if not host:
         return
     hdrs = glob.glob(os.path.join(INCLUDE, "**", "*.h"), recursive=True)
@@ -71,14 +74,18 @@ def build_cxx(force: bool = False) -> None:
     if force or _stale(CXX_LIB, host + hdrs + [CUDA_LIB]):
         _run([HOSTCXX, *common, "-fPIC", "-shared", "-o", CXX_LIB, *host, "-L" + LIB, "-lpowersparse_b200",
               "-L" + CUDA_LIBDIR, "-lcudart", "-Wl,-rpath,$ORIGIN", "-Wl,-rpath," + CUDA_LIBDIR])
-    if cli:
-        os.makedirs(BIN, exist_ok=True)
-        for op, define in (("spmm", []), ("sddmm", ["-DPOWERSPARSE_BENCH_SDDMM=1"])):
-            target = os.path.join(BIN, f"powersparse_{op}")
-            if force or _stale(target, cli + hdrs + [CXX_LIB]):
-                _run([HOSTCXX, *common, *define, "-o", target, *cli, "-L" + LIB, "-lpowersparse",
-                      "-lpowersparse_b200", "-L" + CUDA_LIBDIR, "-lcudart",
-                      "-Wl,-rpath,$ORIGIN/../lib", "-Wl,-rpath," + CUDA_LIBDIR])
+    cli_hdrs = hdrs + [os.path.join(CSRC, "cli", "matrix_market.h")]
+    os.makedirs(BIN, exist_ok=True)
+    for op, define in (("spmm", []), ("sddmm", ["-DPOWERSPARSE_BENCH_SDDMM=1"])):
+        target = os.path.join(BIN, f"powersparse_{op}")
+        if force or _stale(target, cli + cli_hdrs + [CXX_LIB]):
+            _run([HOSTCXX, *common, "-O3", "-pthread", *define, "-o", target, *cli, "-L" + LIB, "-lpowersparse",
+                  "-lpowersparse_b200", "-L" + CUDA_LIBDIR, "-lcudart",
+                  "-Wl,-rpath,$ORIGIN/../lib", "-Wl,-rpath," + CUDA_LIBDIR])
+    # MatrixMarket -> binary CSR converter (host only, no CUDA).
+    target = os.path.join(BIN, "powersparse_mtx2csr")
+    if force or _stale(target, convert + cli_hdrs):
+        _run([HOSTCXX, "-std=c++17", "-O3", "-pthread", "-o", target, *convert])
 
 
 def build_all(force: bool = False) -> None:
