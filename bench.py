@@ -10,21 +10,33 @@ nnz-balanced row panels, and B (all N x 2.45M rows) is replicated (weak
 scaling; no collective in the timed region).  Inputs are larger than L2
 (B is 1.25 GB per 2.45M rows), so no explicit L2 flush is done.
 
-The JSON line's "extra" object times the other operators of the path (SpMM at
-N=32, SDDMM at N=32 and 128) on the same panel with the same rules.
+After the timed steps every rank checks a seeded sample of its panel's rows
+against an FP64 product computed on the host with numpy ("check").  The JSON
+line's "extra" object times the other operators of the path (SpMM at N=32,
+SDDMM at N=32 and 128, the CSR-order and attention-chain additions) on the same
+panel with the same rules, and configuration 5 (R-MAT, 16.8M nodes, ~1B nnz)
+split over the N GPUs (strong scaling), with its own sampled check and the
+all-gather of C.  "e2e" is the same SpMM through the library with host buffers:
+at one GPU B is uploaded whole every step; at N GPUs every rank uploads 1/N of
+B and the GPUs all-gather it over NVLink (NCCL) before the SpMM, and every rank
+reads back its own C panel.
 
-Prints one JSON line (rank 0).  ``--impl reference`` times the reference's CPU
-path (its FP64 CheckSpmm loop, benchmarks/benchmark.cu:64-77, restated in
-oracle/ps_oracle.cpp) on all host cores on the same workload.
+``--impl reference`` times the reference's CPU path (its FP64 CheckSpmm loop,
+benchmarks/benchmark.cu:64-77, restated in oracle/ps_oracle.cpp) on all host
+cores, on row samples of the same global workload, and -- at one GPU, when the
+reference was compiled from its sources into oracle/_ref -- the reference's own
+GPU kernels on the same matrix ("extra.ref_gpu").
 """
 from __future__ import annotations
 
 import argparse
+import hashlib
 import json
 import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import threading
 import time
 
@@ -35,6 +47,15 @@ sys.path.insert(0, ROOT)
 
 METRIC = "SpMM/SDDMM GFLOPS and HBM GB/s (% of roofline) at N=32/128, 1/2/4/8 B200"
 FALLBACK_HBM_GBS = 6650.0
+KERNEL_SOURCE = os.path.join(ROOT, "powersparse_b200", "csrc", "ps_ops.cu")
+ATOL, RTOL = 1e-5, 1e-4  # |a - e| <= ATOL + RTOL * |e| against FP64
+
+
+def host_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
 
 
 def measured_peaks() -> tuple[float, str]:
@@ -46,14 +67,23 @@ def measured_peaks() -> tuple[float, str]:
         return FALLBACK_HBM_GBS, "fallback"
 
 
+def kernel_source_digest() -> str:
+    with open(KERNEL_SOURCE, "rb") as f:
+        return hashlib.sha256(f.read()).hexdigest()[:16]
+
+
 def profile_traffic(kernel: str, workload: str):
-    """DRAM bytes per launch from a committed ncu summary, if one exists for this workload."""
+    """DRAM bytes per launch from profiles/traffic.json, used only when the capture was
+    taken from this build's kernel source (its ps_ops.cu digest); else (None, reason)."""
     p = os.path.join(ROOT, "profiles", "traffic.json")
     try:
         with open(p) as f:
-            return json.load(f)[kernel][workload]
+            entry = json.load(f)[kernel][workload]
     except Exception:
-        return None
+        return None, "no capture for this workload"
+    if not isinstance(entry, dict) or entry.get("ps_ops_sha") != kernel_source_digest():
+        return None, "capture is of another build of ps_ops.cu"
+    return float(entry["bytes"]), f"ncu capture of this build ({entry.get('command', '')})"
 
 
 class ClockSampler:
@@ -119,40 +149,68 @@ class ClockSampler:
                 "samples": len(mhz)}
 
 
+def partition_rows_np(row_ptr: np.ndarray, parts: int) -> np.ndarray:
+    """nnz-balanced contiguous row panels (the rule of ps_partition_rows, in numpy):
+    cut p is the first row whose row_ptr reaches p * nnz / parts."""
+    rp = np.asarray(row_ptr, dtype=np.int64)
+    rows, nnz = len(rp) - 1, int(rp[-1])
+    cuts = np.zeros(parts + 1, dtype=np.int64)
+    for p in range(1, parts):
+        r = int(np.searchsorted(rp, p * nnz // parts, side="left"))
+        cuts[p] = min(max(r, int(cuts[p - 1])), rows)
+    cuts[parts] = rows
+    return cuts
+
+
+def global_graph(workload: str, world: int, device):
+    """(nodes, unique pairs on `device`) of the benchmark graph for this world size:
+    config 2's degree law with world x 2.45M nodes, or the config-5 R-MAT graph."""
+    from powersparse_b200 import synth_gpu
+    if workload == "cfg5":
+        return synth_gpu.config5_pairs(device=device)
+    return synth_gpu.config2_pairs(nodes_scale=world, device=device)
+
+
 def build_workload(rank: int, world: int, device, workload: str = "cfg2"):
     import powersparse_b200 as psb
     from powersparse_b200 import synth_gpu
-    if workload == "cfg5":
-        n_nodes, pairs = synth_gpu.config5_pairs(device=device)   # one graph for every N (strong scaling)
-    else:
-        n_nodes, pairs = synth_gpu.config2_pairs(nodes_scale=world, device=device)
-    cuts = psb.partition_rows(synth_gpu.global_row_ptr(pairs, n_nodes).astype(np.int32), world)
+    n_nodes, pairs = global_graph(workload, world, device)
+    grp = synth_gpu.global_row_ptr(pairs, n_nodes)
+    cuts = psb.partition_rows(grp.astype(np.int32), world)
     panel = synth_gpu.panel_from_pairs(pairs, n_nodes, int(cuts[rank]), int(cuts[rank + 1]),
                                        seed=5 if workload == "cfg5" else 2)
     del pairs
-    return panel, cuts
+    return panel, cuts, int(grp[-1])
 
 
-def dense_B(cols: int, n: int, device):
+def dense_B(cols: int, n: int, device, seed: int = 102):
     import torch
     g = torch.Generator(device=device)
-    g.manual_seed(102)
+    g.manual_seed(seed)
     return torch.rand((cols, n), generator=g, device=device, dtype=torch.float32) * 2 - 1
 
 
-def cpu_spmm_rate(panel, B_host: np.ndarray, min_seconds: float, max_passes: int):
-    """FP64 CheckSpmm restatement on all host cores; returns (GFLOP/s, threads, passes, seconds)."""
-    from oracle import oracle
-    threads = oracle.lib().ps_oracle_max_threads()
-    n = B_host.shape[1]
-    passes, t = 0, 0.0
-    while passes < max_passes and (passes == 0 or t < min_seconds):
-        t0 = time.perf_counter()
-        oracle.spmm(panel.row_ptr, panel.col_ind, panel.values, B_host, threads=threads)
-        t += time.perf_counter() - t0
-        passes += 1
-    flops = 2.0 * panel.nnz * n * passes
-    return flops / t / 1e9, threads, passes, t
+def sampled_check(panel, B, C, rows: int = 2048, seed: int = 7) -> dict:
+    """Rows of C (device) against an FP64 product computed on the host for a seeded
+    sample of the panel's rows: C[r] = sum_p values[p] * B[col_ind[p]] over row r."""
+    import torch
+    rng = np.random.default_rng(seed)
+    r = np.unique(rng.integers(0, panel.rows, size=min(rows, panel.rows)))
+    rp = panel.row_ptr.astype(np.int64)
+    lens = rp[r + 1] - rp[r]
+    idx = np.concatenate([np.arange(rp[x], rp[x + 1]) for x in r]) if lens.sum() else np.zeros(0, np.int64)
+    dev = B.device
+    expected = np.zeros((len(r), B.shape[1]), dtype=np.float64)
+    if len(idx):
+        cols = torch.from_numpy(panel.col_ind[idx].astype(np.int64)).to(dev)
+        Bg = B.index_select(0, cols).double().cpu().numpy()
+        prod = panel.values[idx].astype(np.float64)[:, None] * Bg
+        nz = lens > 0
+        starts = np.concatenate([[0], np.cumsum(lens)[:-1]])[nz]
+        expected[nz] = np.add.reduceat(prod, starts, axis=0)
+    actual = C.index_select(0, torch.from_numpy(r.astype(np.int64)).to(dev)).double().cpu().numpy()
+    bad = int((~(np.isfinite(actual) & (np.abs(actual - expected) <= ATOL + RTOL * np.abs(expected)))).sum())
+    return {"rows": int(len(r)), "elements": int(actual.size), "bad": bad}
 
 
 def main() -> None:
@@ -164,17 +222,22 @@ def main() -> None:
     ap.add_argument("--n", type=int, default=128)
     ap.add_argument("--e2e-steps", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-cfg5", action="store_true", help="skip the configuration-5 extra")
     ap.add_argument("--workload", choices=["cfg2", "cfg5"], default="cfg2",
                     help="cfg2: config 2 per GPU (weak scaling, default); cfg5: the config-5 R-MAT graph "
                          "(16.8M nodes, ~1B nnz) split over the GPUs (strong scaling)")
-    ap.add_argument("--gather", action="store_true",
-                    help="also time the all-gather of the C panels (NCCL) that a replicated result needs")
     args = ap.parse_args()
 
-    import torch
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        # Rank 0 alone runs the reference's CPU path; the other ranks have no work.
+        if rank == 0:
+            run_reference_arm(args, world, local)
+        return
+
+    import torch
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
     dist = None
@@ -183,16 +246,9 @@ def main() -> None:
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=device)
 
-    N = args.n
-    if args.impl == "reference":
-        if rank == 0:
-            run_reference_arm(args, world, device)
-        if dist:
-            dist.destroy_process_group()
-        return
-
     import powersparse_b200 as psb
-    panel, cuts = build_workload(rank, world, device, args.workload)
+    N = args.n
+    panel, cuts, nnz_total = build_workload(rank, world, device, args.workload)
     m = psb.PowerSparseMatrixGPU(panel.rows, panel.cols, panel.nnz, panel.row_ptr, panel.col_ind, panel.values)
     if rank == 0:
         B = dense_B(panel.cols, N, device)
@@ -202,6 +258,45 @@ def main() -> None:
         dist.broadcast(B, 0)  # replicate the dense operand once (setup, untimed)
     C = torch.zeros((panel.rows, N), dtype=torch.float32, device=device)
     stream = torch.cuda.current_stream(device)
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+
+    def max_over_ranks(x: float) -> float:
+        if not dist:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum_over_ranks(x: int) -> int:
+        if not dist:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=device)
+        dist.all_reduce(t)
+        return int(t.item())
+
+    def timed(fn, k):
+        for _ in range(3):
+            fn()
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+        ev0.record(stream)
+        for _ in range(k):
+            fn()
+        ev1.record(stream)
+        torch.cuda.synchronize(device)
+        return max_over_ranks(ev0.elapsed_time(ev1) / k)
+
+    def check_all(panel_, B_, C_, N_, m_):
+        """One fresh SpMM into C_, then every rank's sampled FP64 check; totals over ranks."""
+        C_.zero_()
+        psb.SpMM(m_, N_, B_, C_, stream)
+        torch.cuda.synchronize(device)
+        c = sampled_check(panel_, B_, C_)
+        tot = {k: sum_over_ranks(v) for k, v in c.items()}
+        tot["status"] = "passed" if tot["bad"] == 0 else "failed"
+        return tot
 
     for _ in range(max(args.warmup, 3)):
         psb.SpMM(m, N, B, C, stream)
@@ -209,8 +304,6 @@ def main() -> None:
 
     sampler = ClockSampler(local).start()
     time.sleep(0.15)
-    ev0 = torch.cuda.Event(enable_timing=True)
-    ev1 = torch.cuda.Event(enable_timing=True)
     if dist:
         dist.barrier()
     torch.cuda.synchronize(device)
@@ -226,57 +319,29 @@ def main() -> None:
     time.sleep(0.1)
     sampler.stop()
     ms_local = ev0.elapsed_time(ev1) / args.steps
-    ms = ms_local
-    nnz_total = panel.nnz
-    if dist:
-        t = torch.tensor([ms_local], dtype=torch.float64, device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-        z = torch.tensor([panel.nnz], dtype=torch.float64, device=device)
-        dist.all_reduce(z)
-        nnz_total = int(z.item())
+    ms = max_over_ranks(ms_local)
     gflops = 2.0 * nnz_total * N / (ms * 1e-3) / 1e9
+    check = check_all(panel, B, C, N, m)
 
     # Roofline of the fused kernel (per GPU): compulsory bytes 8*nnz + 4*N*(rows + cols).
     alg_bytes = 8.0 * panel.nnz + 4.0 * N * (panel.rows + panel.cols)
     peak, peak_kind = measured_peaks()
     achieved = alg_bytes / (ms_local * 1e-3) / 1e9
     scaling = "strong" if args.workload == "cfg5" else "weak"
-    traffic = profile_traffic("spmm_fused", f"{args.workload}_spmm_n{N}") if world == 1 else None
+    traffic, traffic_note = (profile_traffic("spmm_fused", f"{args.workload}_spmm_n{N}") if world == 1
+                             else (None, "no capture for multi-GPU panels"))
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "peak_source": peak_kind,
-                "traffic": traffic, "alg_bytes_per_launch": alg_bytes}
+                "traffic": traffic, "traffic_source": traffic_note, "alg_bytes_per_launch": alg_bytes}
     if traffic:
-        # The DRAM bytes the ncu capture measured per launch, over this run's launch time:
-        # how close the gathers run to the measured HBM peak.
         roofline["dram_achieved"] = round(traffic / (ms_local * 1e-3) / 1e9, 1)
         roofline["dram_frac"] = round(traffic / (ms_local * 1e-3) / 1e9 / peak, 4)
     # Model, not roofline: every element gathers its dense row with no reuse.
     roofline["no_reuse_gather_model_gbs"] = round(
         (8.0 * panel.nnz + 4.0 * N * panel.nnz + 4.0 * N * panel.rows) / (ms_local * 1e-3) / 1e9, 1)
 
-    # The other operators of the path on the same panel (kernel only, same timing rules):
-    # SpMM at N=32 and SDDMM at N=32/128 (the reference's N choices).
+    # The other operators of the path on the same panel (kernel only, same timing rules).
     extra = {}
-
-    def timed(fn, k):
-        for _ in range(3):
-            fn()
-        if dist:
-            dist.barrier()
-        torch.cuda.synchronize(device)
-        ev0.record(stream)
-        for _ in range(k):
-            fn()
-        ev1.record(stream)
-        torch.cuda.synchronize(device)
-        t = ev0.elapsed_time(ev1) / k
-        if dist:
-            tt = torch.tensor([t], dtype=torch.float64, device=device)
-            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-            t = float(tt.item())
-        return t
-
     k_extra = max(10, min(args.steps, 50))
     if N != 32:
         B32 = B[:, :32].contiguous()
@@ -284,7 +349,8 @@ def main() -> None:
         ms32 = timed(lambda: psb.SpMM(m, 32, B32, C32, stream), k_extra)
         ab32 = 8.0 * panel.nnz + 4.0 * 32 * (panel.rows + panel.cols)
         extra["spmm_n32"] = {"ms": round(ms32, 4), "gflops": round(2.0 * nnz_total * 32 / (ms32 * 1e-3) / 1e9, 1),
-                             "roofline_frac": round(ab32 / (ms32 * 1e-3) / 1e9 / peak, 4)}
+                             "roofline_frac": round(ab32 / (ms32 * 1e-3) / 1e9 / peak, 4),
+                             "check": check_all(panel, B32, C32, 32, m)["status"]}
         del B32, C32
     outs = [torch.zeros(max(m.workset_size(s), 1), dtype=torch.float32, device=device)
             for s in range(m.GroupTypeNum())]
@@ -328,7 +394,7 @@ def main() -> None:
                              "gb_per_s": round(panel.nnz * 4 * 5 / (ms_sm * 1e-3) / 1e9, 1)}
     del w_csr, C_v
 
-    if args.gather and world > 1:
+    if world > 1:
         # Replicated result: all-gather the C panels over NCCL (outside the timed steps).
         from powersparse_b200.distributed import allgather_rows
         full = allgather_rows(C, cuts)
@@ -336,11 +402,75 @@ def main() -> None:
         extra["allgather_c"] = {"ms": round(tg, 3), "bytes_per_gpu_in": int(full.numel() * 4 - C.numel() * 4)}
         del full
 
-    # End to end through the public API with host buffers, pipelined the way a serving
-    # loop runs it: every step copies its B in from pinned host memory, zeroes C, runs
-    # SpMM and copies its C back out; two buffer sets on three streams let step i+1's
-    # upload overlap step i's readback (PCIe is full duplex).  Per-step bytes are
-    # unchanged.
+    if world == 1:
+        e2e = e2e_whole(psb, m, panel, B, C, N, device, stream, args.e2e_steps, nnz_total)
+    else:
+        e2e = e2e_sharded(psb, m, panel, B, N, rank, world, device, stream, dist, args.e2e_steps, nnz_total,
+                          max_over_ranks)
+
+    cpu = None
+    hB = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        hB = B.cpu().numpy()
+        rate, threads, passes, secs = cpu_spmm_rate(panel, hB, min_seconds=10.0, max_passes=40)
+        cpu = {"value": round(rate, 2), "unit": "GFLOP/s", "cores": threads, "kind": "port",
+               "sample": f"full cfg2 SpMM N={N} (FP64 CheckSpmm restatement, OpenMP), {passes} passes, {secs:.1f} s"}
+    launches = args.steps * (2 if m.wide_rows > 0 else 1)  # spmm_fused (+ wide_rows_fold) per step
+    rows_per_gpu, cols, nnz_rank0, S, pre_ms = panel.rows, panel.cols, panel.nnz, m.GroupTypeNum(), m.preprocess_ms
+    m.close()
+    del B, C, panel, hB
+    torch.cuda.empty_cache()
+
+    if args.workload == "cfg2" and not args.no_cfg5:
+        extra["cfg5"] = run_cfg5(psb, rank, world, device, stream, timed, check_all, dist)
+
+    if rank == 0:
+        clocks = sampler.summary()
+        line = {
+            "metric": METRIC, "value": round(gflops, 1), "unit": "GFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": (f"cfg2: SpMM N={N}, symmetric Chung-Lu gamma=2.1, {world}x2.45M nodes, "
+                                    f"nnz-balanced row panel per GPU, B replicated") if args.workload == "cfg2" else
+                                   (f"cfg5: SpMM N={N}, R-MAT scale 24 edge factor 64 symmetrised, split into {world} "
+                                    f"nnz-balanced row panels, B replicated"),
+                       "rows_per_gpu": rows_per_gpu, "cols": cols, "nnz_per_gpu_rank0": nnz_rank0,
+                       "nnz_total": nnz_total, "N": N, "S": S,
+                       "parallelism": f"row-panel x{world}", "l2": "inputs larger than L2 (B >= 1.25 GB), no flush",
+                       "preprocess_ms": round(pre_ms, 1)},
+            "check": check["status"], "check_detail": check,
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+            "gpu_launches": launches,
+            "clocks": clocks, "extra": extra,
+        }
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def cpu_spmm_rate(panel, B_host: np.ndarray, min_seconds: float, max_passes: int):
+    """FP64 CheckSpmm restatement on all host cores; returns (GFLOP/s, threads, passes, seconds)."""
+    from oracle import oracle
+    threads = host_cores()
+    n = B_host.shape[1]
+    passes, t = 0, 0.0
+    while passes < max_passes and (passes == 0 or t < min_seconds):
+        t0 = time.perf_counter()
+        oracle.spmm(panel.row_ptr, panel.col_ind, panel.values, B_host, threads=threads)
+        t += time.perf_counter() - t0
+        passes += 1
+    flops = 2.0 * panel.nnz * n * passes
+    return flops / t / 1e9, threads, passes, t
+
+
+def e2e_whole(psb, m, panel, B, C, N, device, stream, steps, nnz_total) -> dict:
+    """One GPU, end to end through the public API with host buffers: every step copies
+    its B in from pinned host memory, zeroes C, runs SpMM and copies C back out; two
+    buffer sets on three streams let step i+1's upload overlap step i's readback
+    (PCIe is full duplex).  Per-step bytes are unchanged by the overlap."""
+    import torch
     hB = B.cpu().pin_memory()
     hC = [torch.empty((panel.rows, N), dtype=torch.float32).pin_memory() for _ in range(2)]
     dB = [torch.empty_like(B) for _ in range(2)]
@@ -349,7 +479,7 @@ def main() -> None:
     ev = lambda: torch.cuda.Event()
     in_done, comp_done, out_done = [ev(), ev()], [ev(), ev()], [ev(), ev()]
 
-    def e2e_step(i):
+    def step(i):
         j = i % 2
         with torch.cuda.stream(s_in):
             s_in.wait_event(comp_done[j])      # SpMM of step i-2 has read dB[j]
@@ -365,95 +495,222 @@ def main() -> None:
             hC[j].copy_(dC[j], non_blocking=True)
             out_done[j].record(s_out)
 
-    def drain():
-        for e in out_done + in_done:
-            stream.wait_event(e)
+    ms = _run_pipeline(step, [in_done, comp_done, out_done], stream, device, steps, None)
+    return {"value": round(2.0 * nnz_total * N / (ms * 1e-3) / 1e9, 2), "unit": "GFLOP/s",
+            "h2d_bytes_per_step": int(hB.numel() * 4), "d2h_bytes_per_step": int(hC[0].numel() * 4),
+            "ms_per_step": round(ms, 3), "steps": steps}
 
+
+def e2e_sharded(psb, m, panel, B, N, rank, world, device, stream, dist, steps, nnz_total, max_over_ranks) -> dict:
+    """N GPUs, end to end: every rank uploads its 1/N slice of B from pinned host
+    memory, the ranks all-gather B over NVLink (NCCL), each runs SpMM on its panel and
+    reads back only its own C panel.  Two buffer sets; upload, all-gather, SpMM and
+    readback of consecutive steps overlap on four streams."""
+    import torch
+    cols = B.shape[0]
+    per = -(-cols // world)
+    lo, hi = rank * per, min(cols, (rank + 1) * per)
+    h_slice = torch.zeros((per, N), dtype=torch.float32).pin_memory()
+    if hi > lo:
+        h_slice[: hi - lo].copy_(B[lo:hi].cpu())
+    d_slice = [torch.empty((per, N), dtype=torch.float32, device=device) for _ in range(2)]
+    d_full = [torch.empty((per * world, N), dtype=torch.float32, device=device) for _ in range(2)]
+    dC = [torch.empty((panel.rows, N), dtype=torch.float32, device=device) for _ in range(2)]
+    hC = [torch.empty((panel.rows, N), dtype=torch.float32).pin_memory() for _ in range(2)]
+    s_in, s_comm, s_out = (torch.cuda.Stream(device) for _ in range(3))
+    ev = lambda: torch.cuda.Event()
+    in_done, gathered, comp_done, out_done = ([ev(), ev()] for _ in range(4))
+
+    def step(i):
+        j = i % 2
+        with torch.cuda.stream(s_in):
+            s_in.wait_event(gathered[j])       # the all-gather of step i-2 has read d_slice[j]
+            d_slice[j].copy_(h_slice, non_blocking=True)
+            in_done[j].record(s_in)
+        with torch.cuda.stream(s_comm):
+            s_comm.wait_event(in_done[j])
+            s_comm.wait_event(comp_done[j])    # SpMM of step i-2 has read d_full[j]
+            dist.all_gather_into_tensor(d_full[j], d_slice[j])
+            gathered[j].record(s_comm)
+        stream.wait_event(gathered[j])
+        stream.wait_event(out_done[j])         # readback of step i-2 has read dC[j]
+        dC[j].zero_()
+        psb.SpMM(m, N, d_full[j], dC[j], stream)
+        comp_done[j].record(stream)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(comp_done[j])
+            hC[j].copy_(dC[j], non_blocking=True)
+            out_done[j].record(s_out)
+
+    ms = max_over_ranks(_run_pipeline(step, [in_done, gathered, comp_done, out_done], stream, device, steps, dist))
+    # Correctness of the assembled operand: the gathered B equals the replicated one.
+    same = bool(torch.equal(d_full[(steps - 1) % 2][:cols], B))
+    return {"value": round(2.0 * nnz_total * N / (ms * 1e-3) / 1e9, 2), "unit": "GFLOP/s",
+            "h2d_bytes_per_step": int(h_slice.numel() * 4), "d2h_bytes_per_step": int(hC[0].numel() * 4),
+            "bytes_per": "rank", "h2d_bytes_per_step_all_ranks": int(h_slice.numel() * 4 * world),
+            "allgather_bytes_in_per_rank": int((world - 1) * per * N * 4),
+            "gathered_B_matches": same, "ms_per_step": round(ms, 3), "steps": steps}
+
+
+def _run_pipeline(step, events, stream, device, steps, dist) -> float:
+    import torch
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
+
+    def drain():
+        for pair in events:
+            for e in pair:
+                stream.wait_event(e)
+
     for i in range(2):
-        e2e_step(i)
+        step(i)
     drain()
     torch.cuda.synchronize(device)
     if dist:
         dist.barrier()
+        torch.cuda.synchronize(device)
     e0.record(stream)
-    for i in range(args.e2e_steps):
-        e2e_step(i)
+    for i in range(steps):
+        step(i)
     drain()
     e1.record(stream)
     torch.cuda.synchronize(device)
-    e2e_ms = e0.elapsed_time(e1) / args.e2e_steps
-    if dist:
-        t = torch.tensor([e2e_ms], dtype=torch.float64, device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
-    e2e = {"value": round(2.0 * nnz_total * N / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GFLOP/s",
-           "h2d_bytes_per_step": int(hB.numel() * 4), "d2h_bytes_per_step": int(hC[0].numel() * 4),
-           "ms_per_step": round(e2e_ms, 3), "steps": args.e2e_steps}
+    return e0.elapsed_time(e1) / steps
 
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        rate, threads, passes, secs = cpu_spmm_rate(panel, hB.numpy(), min_seconds=10.0, max_passes=40)
-        cpu = {"value": round(rate, 2), "unit": "GFLOP/s", "cores": threads, "kind": "port",
-               "sample": f"full cfg2 SpMM N={N} (FP64 CheckSpmm restatement, OpenMP), {passes} passes, {secs:.1f} s"}
 
-    if rank == 0:
-        clocks = sampler.summary()
-        line = {
-            "metric": METRIC, "value": round(gflops, 1), "unit": "GFLOP/s", "n_gpus": world,
-            "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": round(ms, 4),
-            "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic",
-            "config": {"workload": (f"cfg2: SpMM N={N}, symmetric Chung-Lu gamma=2.1, {world}x2.45M nodes, "
-                                    f"nnz-balanced row panel per GPU, B replicated") if args.workload == "cfg2" else
-                                   (f"cfg5: SpMM N={N}, R-MAT scale 24 edge factor 64 symmetrised, split into {world} "
-                                    f"nnz-balanced row panels, B replicated"),
-                       "rows_per_gpu": panel.rows, "cols": panel.cols, "nnz_per_gpu_rank0": panel.nnz,
-                       "nnz_total": nnz_total, "N": N, "S": m.GroupTypeNum(),
-                       "parallelism": f"row-panel x{world}", "l2": "inputs larger than L2 (B >= 1.25 GB), no flush",
-                       "preprocess_ms": round(m.preprocess_ms, 1)},
-            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
-            # per step: spmm_fused, plus wide_rows_fold when the panel has wide rows
-            "gpu_launches": args.steps * (2 if m.wide_rows > 0 else 1),
-            "clocks": clocks, "extra": extra,
-        }
-        print(json.dumps(line), flush=True)
+def run_cfg5(psb, rank, world, device, stream, timed, check_all, dist, steps: int = 20) -> dict:
+    """Configuration 5 (R-MAT scale 24, edge factor 64, ~1B nnz) split into `world`
+    nnz-balanced row panels (strong scaling): SpMM N=128 per step, its sampled check,
+    and the all-gather of the C panels into a replicated result."""
+    import torch
+    t0 = time.time()
+    panel, cuts, nnz_total = build_workload(rank, world, device, "cfg5")
+    torch.cuda.empty_cache()
+    m = psb.PowerSparseMatrixGPU(panel.rows, panel.cols, panel.nnz, panel.row_ptr, panel.col_ind, panel.values)
+    B = dense_B(panel.cols, 128, device, seed=105)  # the same replicated B on every rank (same seed)
+    C = torch.zeros((panel.rows, 128), dtype=torch.float32, device=device)
+    ms = timed(lambda: psb.SpMM(m, 128, B, C, stream), steps)
+    check = check_all(panel, B, C, 128, m)
+    out = {"workload": "cfg5: R-MAT scale 24 (16,777,216 nodes), edge factor 64, symmetrised, "
+                       f"{world} row panels, SpMM N=128, B replicated",
+           "scaling": "strong", "nnz_total": nnz_total, "nnz_rank0": panel.nnz, "rows_rank0": panel.rows,
+           "ms": round(ms, 4), "gflops": round(2.0 * nnz_total * 128 / (ms * 1e-3) / 1e9, 1),
+           "preprocess_ms_rank0": round(m.preprocess_ms, 1), "check": check["status"], "check_detail": check,
+           "steps": steps}
+    if world > 1:
+        from powersparse_b200.distributed import allgather_rows
+        full = allgather_rows(C, cuts)
+        out["allgather_c_ms"] = round(timed(lambda: allgather_rows(C, cuts), 3), 3)
+        out["allgather_bytes_in_per_gpu"] = int(full.numel() * 4 - C.numel() * 4)
+        del full
+    out["setup_s"] = round(time.time() - t0, 1)
     m.close()
-    if dist:
-        dist.barrier()
-        dist.destroy_process_group()
+    del B, C, panel
+    torch.cuda.empty_cache()
+    return out
 
 
-def run_reference_arm(args, world: int, device) -> None:
-    """The reference's CPU path (FP64 CheckSpmm, restated: no separately callable CPU
-    SpMM exists in the reference) on all host cores, on rank 0's panel of the same workload."""
-    panel, _ = build_workload(0, world, device, args.workload)
-    N = args.n
-    B = dense_B(panel.cols, N, device).cpu().numpy()
+def run_reference_arm(args, world: int, local: int) -> None:
+    """The reference's CPU path (FP64 CheckSpmm, restated: the reference has no
+    separately callable CPU SpMM) on all host cores.  The workload is the repo arm's
+    global graph at this world size (every rank's panel); each step multiplies a
+    bounded sample of it: from every nnz-balanced panel a contiguous block of rows
+    (rotating from step to step), about 16M nonzeros in total, against the full B.
+    Inputs are generated with torch on GPU `local`; the product library is not loaded."""
+    import torch
     from oracle import oracle
-    threads = oracle.lib().ps_oracle_max_threads()
-    for _ in range(min(args.warmup, 1)):
-        oracle.spmm(panel.row_ptr, panel.col_ind, panel.values, B, threads=threads)
-    times = []
-    for _ in range(args.steps):
+    from powersparse_b200 import synth_gpu
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    N = args.n
+    threads = host_cores()
+    n_nodes, pairs = global_graph(args.workload, world, device)
+    full = synth_gpu.panel_from_pairs(pairs, n_nodes, 0, n_nodes, seed=5 if args.workload == "cfg5" else 2)
+    del pairs
+    torch.cuda.empty_cache()
+    cuts = partition_rows_np(full.row_ptr, world)
+    B = dense_B(n_nodes, N, device).cpu().numpy()
+    rp = full.row_ptr.astype(np.int64)
+    target = 16_000_000 // world
+
+    def blocks(step: int):
+        out = []
+        for p in range(world):
+            r0, r1 = int(cuts[p]), int(cuts[p + 1])
+            if r1 <= r0:
+                continue
+            span = r1 - r0
+            start = r0 + (step * 7919 * 1031) % span
+            end = int(np.searchsorted(rp, rp[start] + target, side="left"))
+            out.append((start, max(start + 1, min(end, r1))))
+        return out
+
+    def run(step: int):
+        nnz = 0
+        for r0, r1 in blocks(step):
+            oracle.spmm_rows(r0, r1, full.row_ptr, full.col_ind, full.values, B, threads=threads)
+            nnz += int(rp[r1] - rp[r0])
+        return nnz
+
+    for w in range(min(args.warmup, 1)):
+        run(10_000 + w)
+    times, nnzs = [], []
+    for s in range(args.steps):
         t0 = time.perf_counter()
-        oracle.spmm(panel.row_ptr, panel.col_ind, panel.values, B, threads=threads)
+        nnzs.append(run(s))
         times.append(time.perf_counter() - t0)
-        if sum(times) > 120:
+        if sum(times) > 60:
             break
-    ms = 1e3 * sum(times) / len(times)
-    v = 2.0 * panel.nnz * N / (ms * 1e-3) / 1e9
+    secs = sum(times)
+    v = 2.0 * sum(nnzs) * N / secs / 1e9
+    ms = 1e3 * secs / len(times)
+    scaling = "strong" if args.workload == "cfg5" else "weak"
+    sample = (f"{len(times)} steps; each multiplies ~16M nonzeros: from each of the {world} nnz-balanced panels of "
+              f"the {int(rp[-1])}-nnz graph a contiguous row block (rotating), against the full B "
+              f"({n_nodes} x {N}); FP64 CheckSpmm restatement, OpenMP")
     line = {"metric": METRIC, "value": round(v, 2), "unit": "GFLOP/s", "n_gpus": world, "steps": len(times),
             "warmup": min(args.warmup, 1), "ms_per_step": round(ms, 2), "higher_is_better": True,
-            "scaling": "strong" if args.workload == "cfg5" else "weak", "vs_baseline": None, "dtype": "f64",
-            "data": "synthetic", "impl": "reference",
-            "config": {"workload": f"{args.workload}: SpMM N={N}, rank-0 row panel ({world} panels)",
-                       "rows": panel.rows, "nnz": panel.nnz, "N": N},
+            "scaling": scaling, "vs_baseline": None, "dtype": "f64", "data": "synthetic", "impl": "reference",
+            "config": {"workload": (f"cfg2: SpMM N={N}, symmetric Chung-Lu gamma=2.1, {world}x2.45M nodes, "
+                                    f"{world} nnz-balanced row panels") if args.workload == "cfg2" else
+                                   f"cfg5: SpMM N={N}, R-MAT scale 24 edge factor 64, {world} row panels",
+                       "nnz_total": int(rp[-1]), "N": N, "threads": threads},
             "cpu_baseline": {"value": round(v, 2), "unit": "GFLOP/s", "cores": threads, "kind": "port",
-                             "sample": f"one row panel ({panel.nnz} nnz) per step, FP64 CheckSpmm restatement"},
+                             "sample": sample},
             "e2e": {"value": round(v, 2), "unit": "GFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    if world == 1 and args.workload == "cfg2":
+        line["extra"] = {"ref_gpu": reference_gpu_times(full)}
     print(json.dumps(line), flush=True)
+
+
+def reference_gpu_times(csr) -> dict:
+    """The reference's own GPU kernels (compiled from its sources into oracle/_ref,
+    called through its public API by oracle/_ref/ps_ref_dump) on the same matrix,
+    timed with the reference's protocol (30 warm-up calls, outputs zeroed, 20 timed
+    calls under one event pair); dense operands generated on the device."""
+    exe = os.path.join(ROOT, "oracle", "_ref", "ps_ref_dump")
+    if not os.path.exists(exe):
+        return {"unavailable": "oracle/_ref/ps_ref_dump was not built (no reference checkout at build time)"}
+    from powersparse_b200 import synth
+    out = {}
+    with tempfile.TemporaryDirectory() as d:
+        path = os.path.join(d, "a.csr")
+        synth.write_csr_bin(path, csr)
+        for op, n in (("spmm", 32), ("spmm", 128), ("sddmm", 32), ("sddmm", 128)):
+            cmd = [exe, op, path, str(n), "@rand:1"] + (["@rand:2"] if op == "sddmm" else []) + ["-", "20"]
+            try:
+                r = subprocess.run(cmd, capture_output=True, text=True, timeout=600)
+                rec = json.loads(r.stdout.strip().splitlines()[-1]) if r.returncode == 0 else None
+            except Exception as e:  # noqa: BLE001 - reported, not raised
+                rec, r = None, None
+                out[f"{op}_n{n}"] = {"error": str(e)[:200]}
+                continue
+            if rec is None:
+                out[f"{op}_n{n}"] = {"error": (r.stderr or r.stdout).strip()[-200:]}
+            else:
+                out[f"{op}_n{n}"] = {"ms": round(rec["ms"], 4), "gflops": round(rec["gflops"], 1),
+                                     "preprocess_ms": round(rec["preprocess_ms"], 1)}
+    return out
 
 
 if __name__ == "__main__":

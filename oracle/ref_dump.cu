@@ -8,7 +8,10 @@
 //   ps_ref_dump spmm   IN.csr N B.f32 OUT.f32 [REPEATS]
 //   ps_ref_dump sddmm  IN.csr N LHS.f32 RHS.f32 OUTPREFIX [REPEATS]
 //
-// IN.csr is the binary CSR written by powersparse_b200.synth.write_csr_bin.
+// IN.csr is the binary CSR written by powersparse_b200.synth.write_csr_bin.  A
+// dense operand given as "@rand:SEED" is generated on the device instead of read
+// (uniform in [-1, 1) from a counter hash; for timing runs), and an output path
+// "-" writes nothing.
 // With REPEATS > 0 the operator is also timed the way benchmarks/benchmark.cu
 // does it (30 warm-up calls, outputs zeroed, REPEATS back-to-back calls under
 // one event pair) and one JSON line is printed.
@@ -87,6 +90,29 @@ T* upload(const std::vector<T>& h) {
   return d;
 }
 
+// Counter hash (splitmix64 finalizer) to [-1, 1): dense operands for timing runs.
+__global__ void fill_uniform(float* out, size_t count, unsigned long long seed) {
+  for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < count; i += size_t(gridDim.x) * blockDim.x) {
+    unsigned long long z = i + 0x9E3779B97F4A7C15ull * (seed + 1);
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    z ^= z >> 31;
+    out[i] = float((z >> 40) * (1.0 / 16777216.0)) * 2.0f - 1.0f;
+  }
+}
+
+float* dense_input(const std::string& spec, size_t count) {
+  if (spec.rfind("@rand:", 0) == 0) {
+    float* d = nullptr;
+    CUDA_CALL(cudaMalloc(&d, sizeof(float) * (count ? count : 1)));
+    fill_uniform<<<1024, 256>>>(d, count, std::stoull(spec.substr(6)));
+    CUDA_CALL(cudaGetLastError());
+    CUDA_CALL(cudaDeviceSynchronize());
+    return d;
+  }
+  return upload(read_raw<float>(spec, count));
+}
+
 size_t workset_size(const PowerSparse::PowerSparseMatrixGPU& m, int s, const std::vector<int>& res) {
   return s == 0 ? size_t(res.back()) : size_t(m.GroupNum()[s]) * GROUP_SIZE(s);
 }
@@ -156,7 +182,7 @@ int run(int argc, char** argv) {
   std::string out_path;
   if (mode == "spmm") {
     if (argc < 6) return 2;
-    d_rhs = upload(read_raw<float>(argv[4], size_t(csr.cols) * n));
+    d_rhs = dense_input(argv[4], size_t(csr.cols) * n);
     out_path = argv[5];
     if (argc > 6) repeats = std::stoi(argv[6]);
     CUDA_CALL(cudaMalloc(&d_c, sizeof(float) * size_t(csr.rows) * n));
@@ -165,8 +191,8 @@ int run(int argc, char** argv) {
     invoke = [&] { PowerSparse::SpMM(m, n, d_rhs, d_c, S, streams.s.data()); };
   } else if (mode == "sddmm") {
     if (argc < 7) return 2;
-    d_lhs = upload(read_raw<float>(argv[4], size_t(csr.rows) * n));
-    d_rhs = upload(read_raw<float>(argv[5], size_t(csr.cols) * n));
+    d_lhs = dense_input(argv[4], size_t(csr.rows) * n);
+    d_rhs = dense_input(argv[5], size_t(csr.cols) * n);
     out_path = argv[6];
     if (argc > 7) repeats = std::stoi(argv[7]);
     for (int s = 0; s < S; ++s) {
@@ -188,7 +214,9 @@ int run(int argc, char** argv) {
   reset();
   invoke();
   CUDA_CALL(cudaDeviceSynchronize());
-  if (mode == "spmm") {
+  if (out_path == "-") {
+    // timing run: nothing written
+  } else if (mode == "spmm") {
     const auto c = download(d_c, out_sizes[0]);
     write_raw(out_path, c.data(), c.size());
   } else {
