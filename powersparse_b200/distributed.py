@@ -12,6 +12,7 @@ CPU tensors).
 """
 from __future__ import annotations
 
+import time
 from typing import Optional
 
 import numpy as np
@@ -19,7 +20,35 @@ import numpy as np
 from . import PowerSparseMatrixGPU, SDDMM, SpMM, partition_rows
 from .synth import Csr
 
-__all__ = ["panel_csr", "ShardedPowerSparse", "allgather_rows"]
+__all__ = ["panel_csr", "ShardedPowerSparse", "allgather_rows", "heartbeat", "PeerLost"]
+
+
+class PeerLost(RuntimeError):
+    """A rank of the process group stopped taking part: it failed, left between
+    steps, or never reached the step."""
+
+
+def heartbeat(step: int, timeout_s: float = 10.0, group=None, store=None) -> None:
+    """Host-side liveness check at the start of a step, before its launches: every
+    rank announces (step, rank) in the process group's key-value store and waits up
+    to ``timeout_s`` seconds for the announcements of the others.  A rank that failed
+    or left between steps is found here, on the host, before this step issues any
+    kernel or collective; raises PeerLost naming the missing ranks.  Every rank must
+    call it with the same step numbers."""
+    import torch.distributed as dist
+    if store is None:
+        store = dist.distributed_c10d._get_default_store()
+    rank, world = dist.get_rank(group), dist.get_world_size(group)
+    store.set(f"psb/heartbeat/{step}/{rank}", "1")
+    deadline = time.monotonic() + timeout_s
+    missing = list(range(world))
+    while True:
+        missing = [r for r in missing if not store.check([f"psb/heartbeat/{step}/{r}"])]
+        if not missing:
+            return
+        if time.monotonic() >= deadline:
+            raise PeerLost(f"rank(s) {missing} did not reach step {step} within {timeout_s:g} s")
+        time.sleep(0.01)
 
 
 def panel_csr(m: Csr, r0: int, r1: int) -> Csr:
@@ -32,7 +61,9 @@ def panel_csr(m: Csr, r0: int, r1: int) -> Csr:
 def allgather_rows(local, cuts, group=None):
     """Concatenate every rank's row panel (``local``: [cuts[r+1]-cuts[r], N]) into the
     full [cuts[-1], N] tensor on every rank.  Panels are padded to the longest one for
-    one ``all_gather_into_tensor``; collective order is the same on every rank."""
+    one ``all_gather_into_tensor``; collective order is the same on every rank.  A
+    collective that fails because a rank is gone (the group's timeout, or a closed
+    connection) raises PeerLost."""
     import torch
     import torch.distributed as dist
     world = dist.get_world_size(group)
@@ -43,8 +74,29 @@ def allgather_rows(local, cuts, group=None):
     padded = torch.zeros((longest, n), dtype=local.dtype, device=local.device)
     padded[: local.shape[0]].copy_(local)
     gathered = torch.empty((world * longest, n), dtype=local.dtype, device=local.device)
-    dist.all_gather_into_tensor(gathered, padded, group=group)
+    try:
+        dist.all_gather_into_tensor(gathered, padded, group=group)
+    except (RuntimeError, dist.DistError) as e:  # a peer failed, left, or the group timed out
+        raise PeerLost(f"all-gather of the row panels failed: {e}") from e
     return torch.cat([gathered[r * longest: r * longest + rows[r]] for r in range(world)])
+
+
+def _current_waits_for(stream, tensor) -> None:
+    """Make torch's current stream on ``tensor``'s device wait for ``stream`` (a
+    torch.cuda.Stream, a raw cudaStream_t as int, or None for the legacy default
+    stream)."""
+    import torch
+    if not tensor.is_cuda:
+        return
+    current = torch.cuda.current_stream(tensor.device)
+    if stream is None:
+        other = torch.cuda.default_stream(tensor.device)
+    elif isinstance(stream, torch.cuda.Stream):
+        other = stream
+    else:
+        other = torch.cuda.ExternalStream(int(stream), device=tensor.device)
+    if other.cuda_stream != current.cuda_stream:
+        current.wait_stream(other)
 
 
 class ShardedPowerSparse:
@@ -67,9 +119,14 @@ class ShardedPowerSparse:
                                            panel.values, sm_count=sm_count)
 
     def spmm(self, N: int, B, C_local, stream=None, gather: bool = False, group=None):
-        """C_local (+)= A_panel · B; with ``gather`` also return the full C on every rank."""
+        """C_local (+)= A_panel · B; with ``gather`` also return the full C on every rank.
+
+        The all-gather is ordered after torch's current stream, so when ``stream`` is
+        another stream the current one first waits for it (the SpMM has finished
+        writing C_local before the gather reads it)."""
         SpMM(self.matrix, N, B, C_local, stream)
         if gather:
+            _current_waits_for(stream, C_local)
             return allgather_rows(C_local, self.cuts, group)
         return C_local
 
