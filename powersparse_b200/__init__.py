@@ -92,11 +92,14 @@ def GROUP_SIZE(s: int) -> int:
     return 32 * (1 << (s - 1))
 
 
-def load_library(path: str = LIB_PATH):
-    """Load the CUDA library (raises if it has not been built)."""
+def load_library(path: Optional[str] = None):
+    """Load the CUDA library (raises if it has not been built).  ``path`` defaults to
+    the ``PSB_LIBRARY`` environment variable, else ``lib/libpowersparse_b200.so``
+    (``lib/libpowersparse_b200_checked.so`` is the bounds-checked debug build)."""
     global _lib
     if _lib is not None:
         return _lib
+    path = path or os.environ.get("PSB_LIBRARY") or LIB_PATH
     if not os.path.exists(path):
         raise RuntimeError(f"{path} is missing: build it with `python -m powersparse_b200.build` "
                            "(there is no host fallback)")

@@ -5,6 +5,7 @@
 
 Outputs (git-ignored, shipped with the tree):
   powersparse_b200/lib/libpowersparse_b200.so  C ABI + CUDA kernels (include/powersparse_b200.h)
+  powersparse_b200/lib/libpowersparse_b200_checked.so   the same with bounds-checked kernels
   powersparse_b200/lib/libpowersparse.so       the reference's C++ operator API over the C ABI
   powersparse_b200/bin/powersparse_spmm        drop-in benchmark CLI (SpMM)
   powersparse_b200/bin/powersparse_sddmm       drop-in benchmark CLI (SDDMM)
@@ -32,6 +33,10 @@ CUDA_LIBDIR = os.path.join(os.path.dirname(os.path.dirname(os.path.realpath(
     "lib64")
 
 CUDA_LIB = os.path.join(LIB, "libpowersparse_b200.so")
+# The same library with every operator kernel checking the indices it follows
+# (-DPSB_BOUNDS_CHECK; see ps_ops.cu).  For debugging: each operator call waits for
+# its kernels.  Load it with PSB_LIBRARY=<path> (powersparse_b200.load_library).
+CHECKED_LIB = os.path.join(LIB, "libpowersparse_b200_checked.so")
 CXX_LIB = os.path.join(LIB, "libpowersparse.so")
 
 
@@ -54,9 +59,10 @@ def build_cuda(force: bool = False) -> str:
     deps = srcs + glob.glob(os.path.join(CSRC, "*.h")) + glob.glob(os.path.join(CSRC, "*.cuh")) + \
         [os.path.join(INCLUDE, "powersparse_b200.h")]
     os.makedirs(LIB, exist_ok=True)
-    if force or _stale(CUDA_LIB, deps):
-        _run([NVCC, "-std=c++17", "-O3", *ARCH, "-lineinfo", "-Xcompiler", "-fPIC", "-shared",
-              "-ccbin", HOSTCXX, "-I" + INCLUDE, "-o", CUDA_LIB, *srcs])
+    for target, flags in ((CUDA_LIB, []), (CHECKED_LIB, ["-DPSB_BOUNDS_CHECK=1"])):
+        if force or _stale(target, deps):
+            _run([NVCC, "-std=c++17", "-O3", *ARCH, "-lineinfo", "-Xcompiler", "-fPIC", "-shared", *flags,
+                  "-ccbin", HOSTCXX, "-I" + INCLUDE, "-o", target, *srcs])
     return CUDA_LIB
 
 

@@ -47,7 +47,49 @@ struct WorksetView {
   const int* des[kMaxWorksets];
   int group_len[kMaxWorksets];
   int groups[kMaxWorksets];
+  long long len[kMaxWorksets];  // elements of the workset
 };
+
+// --- Bounds-checked build ------------------------------------------------------
+// With PSB_BOUNDS_CHECK defined (lib/libpowersparse_b200_checked.so, built by
+// `python -m powersparse_b200.build`), the operator kernels check every index they
+// take from the layout, the task lists or a caller's array before following it.  A
+// bad task is skipped and a bad index is not followed (the access is dropped or
+// redirected to element 0); the first failure is recorded in g_bounds_status, and the
+// launcher waits for the launch and raises it as an error.  No assert or trap: the
+// context stays usable.  The release library compiles every check away.
+#ifdef PSB_BOUNDS_CHECK
+constexpr bool kChecked = true;
+#else
+constexpr bool kChecked = false;
+#endif
+
+enum BoundsCode : unsigned {
+  kBadTask = 1,      // task outside its workset, or an unknown workset / group / slot
+  kBadColumn = 2,    // column index >= cols
+  kBadRow = 3,       // destination row >= rows
+  kBadGroup = 4,     // group index past the workset's groups
+  kBadPosition = 5,  // CSR position >= nnz
+  kBadRowPtr = 6,    // row pointer out of order or past nnz
+};
+
+__device__ unsigned long long g_bounds_status;  // (code << 32) | low bits of the bad index; 0: none
+
+// True when 0 <= v < limit; otherwise (checked build) records the failure.
+__device__ __forceinline__ bool in_range(long long v, long long limit, unsigned code) {
+  if constexpr (kChecked) {
+    if (v < 0 || v >= limit) {
+      atomicCAS(&g_bounds_status, 0ull, ((unsigned long long)code << 32) | (unsigned long long)(v & 0xffffffffLL));
+      return false;
+    }
+  }
+  return true;
+}
+
+// v when it is in [0, limit); otherwise (checked build) 0, with the failure recorded.
+__device__ __forceinline__ long long checked(long long v, long long limit, unsigned code) {
+  return in_range(v, limit, code) ? v : 0;
+}
 
 __device__ __forceinline__ void fma4(float4& acc, float s, const float4& b) {
   acc.x = fmaf(s, b.x, acc.x);
@@ -89,7 +131,23 @@ struct SpmmArgs {
   double* wide_acc;  // [wide rows][N] FP64 slice sums (tasks with slot >= 0)
   const int* pos_ws[kMaxWorksets];  // CSR position of every element (kValues)
   const float* values;              // per-call values in CSR order (kValues)
+  int S, rows, cols, nnz, wide_rows;  // index limits (checked build)
 };
+
+// Checked build: a task must lie inside its workset (begin <= end <= workset length,
+// group < groups) and name an existing wide-row slot.
+template <typename Args>
+__device__ __forceinline__ bool task_ok(const Args& a, const Task& t) {
+  if constexpr (kChecked) {
+    if (!in_range(t.ws, a.S, kBadTask)) return false;
+    const long long len = a.ws.len[t.ws];
+    if (!in_range(t.begin, len + 1, kBadTask) || !in_range(t.end, len + 1, kBadTask) ||
+        !in_range(t.end - t.begin, len + 1, kBadTask) || !in_range(t.group, max(a.ws.groups[t.ws], 1), kBadTask))
+      return false;
+    if (t.slot >= 0 && !in_range(t.slot, a.wide_rows, kBadTask)) return false;
+  }
+  return true;
+}
 
 // SpMM, one task per lane group:
 //   C[row(g), slab] (+)= sum over elements e of group g of val[e] * B[col[e], slab].
@@ -120,6 +178,7 @@ __global__ void __launch_bounds__(kThreads, 4) spmm_fused(const SpmmArgs a) {
   const int task_id = (blockIdx.x * kWarpsPerBlock + warp) * NG + q;
   if (task_id >= a.num_tasks) return;
   const Task t = task_id < a.num_block ? a.block_tasks[task_id] : a.res_tasks[task_id - a.num_block];
+  if (!task_ok(a, t)) return;
   const int* __restrict__ col = a.ws.col[t.ws];
   const float* __restrict__ val = a.ws.val[t.ws];
   const int* __restrict__ des = a.ws.des[t.ws];
@@ -129,16 +188,21 @@ __global__ void __launch_bounds__(kThreads, 4) spmm_fused(const SpmmArgs a) {
   int* sc = s_col[warp][q];
   float* sv = s_val[warp][q];
   int2* cv = s_cv[kPairs ? warp : 0];
-  auto gather = [&](int c) { return __ldg(reinterpret_cast<const float4*>(Bl + (long long)c * a.ldb)); };
+  auto gather = [&](int c) {
+    return __ldg(reinterpret_cast<const float4*>(Bl + checked(c, a.cols, kBadColumn) * a.ldb));
+  };
   const int* __restrict__ pos = a.pos_ws[t.ws];
   auto value1 = [&](int e) -> float {
-    if constexpr (kValues) return __ldg(a.values + __ldcs(pos + e));
+    if constexpr (kValues) return __ldg(a.values + checked(__ldcs(pos + e), a.nnz, kBadPosition));
     else return __ldcs(val + e);
   };
   auto value4 = [&](int e0, int k) -> float4 {  // elements e0 + 4k .. e0 + 4k + 3, e0 16-byte aligned
     if constexpr (kValues) {
       const int4 p = __ldcs(reinterpret_cast<const int4*>(pos + e0) + k);
-      return make_float4(__ldg(a.values + p.x), __ldg(a.values + p.y), __ldg(a.values + p.z), __ldg(a.values + p.w));
+      return make_float4(__ldg(a.values + checked(p.x, a.nnz, kBadPosition)),
+                         __ldg(a.values + checked(p.y, a.nnz, kBadPosition)),
+                         __ldg(a.values + checked(p.z, a.nnz, kBadPosition)),
+                         __ldg(a.values + checked(p.w, a.nnz, kBadPosition)));
     } else {
       return __ldcs(reinterpret_cast<const float4*>(val + e0) + k);
     }
@@ -198,7 +262,7 @@ __global__ void __launch_bounds__(kThreads, 4) spmm_fused(const SpmmArgs a) {
         for (int u = 0; u < kUnroll; ++u) {
           if (j + u < n) {
             if (base + j + u == cur_end) {
-              emit4(Cl + (long long)cur_row * a.ldb, acc, cur_atomic);
+              if (in_range(cur_row, a.rows, kBadRow)) emit4(Cl + (long long)cur_row * a.ldb, acc, cur_atomic);
               acc = make_float4(0.f, 0.f, 0.f, 0.f);
               if (++widx == LG) {
                 wbase += LG;
@@ -219,7 +283,7 @@ __global__ void __launch_bounds__(kThreads, 4) spmm_fused(const SpmmArgs a) {
       }
       __syncwarp(gm);
     }
-    emit4(Cl + (long long)cur_row * a.ldb, acc, cur_atomic);
+    if (in_range(cur_row, a.rows, kBadRow)) emit4(Cl + (long long)cur_row * a.ldb, acc, cur_atomic);
     return;
   }
 
@@ -329,7 +393,8 @@ __global__ void __launch_bounds__(kThreads, 4) spmm_fused(const SpmmArgs a) {
         atomicAdd(row_sum + 2, dz);
         atomicAdd(row_sum + 3, dw);
       } else {
-        emit4(Cl + (long long)des[g] * a.ldb, make_float4(float(dx), float(dy), float(dz), float(dw)), true);
+        if (in_range(g, a.ws.groups[t.ws], kBadGroup) && in_range(des[g], a.rows, kBadRow))
+          emit4(Cl + (long long)des[g] * a.ldb, make_float4(float(dx), float(dy), float(dz), float(dw)), true);
       }
       dx = dy = dz = dw = 0.0;
       ++g;
@@ -349,6 +414,7 @@ struct SddmmArgs {
   float* out_ws[kMaxWorksets];
   const int* pos_ws[kMaxWorksets];  // CSR position of every element (CSR-order output)
   float* out_csr;                   // CSR-order output, or nullptr
+  int S, rows, cols, nnz, wide_rows;  // index limits (checked build)
 };
 
 // Reduces BATCH per-lane partial dot products over the LG lanes of a lane group:
@@ -408,6 +474,7 @@ __global__ void __launch_bounds__(kThreads, LG == 8 ? 4 : 3) sddmm_fused(const S
   const int task_id = (blockIdx.x * kWarpsPerBlock + warp) * NG + q;
   if (task_id >= a.num_tasks) return;
   const Task t = task_id < a.num_block ? a.block_tasks[task_id] : a.res_tasks[task_id - a.num_block];
+  if (!task_ok(a, t)) return;
   const int* __restrict__ col = a.ws.col[t.ws];
   const float* __restrict__ val = a.ws.val[t.ws];
   float* __restrict__ out = a.out_ws[t.ws];
@@ -417,8 +484,9 @@ __global__ void __launch_bounds__(kThreads, LG == 8 ? 4 : 3) sddmm_fused(const S
   int* sc = s_col[warp][q];
   float* sv = s_val[warp][q];
   int* sr = s_row[warp][q];
-  auto seg = [](const float* base, long long row, int c) {
-    return __ldg(reinterpret_cast<const float4*>(base + row * N + c * SEG));
+  // Segment c of dense row `row` (< limit) of lhs or rhs.
+  auto seg = [](const float* base, long long row, int c, long long limit, unsigned code) {
+    return __ldg(reinterpret_cast<const float4*>(base + checked(row, limit, code) * N + c * SEG));
   };
 
   if (t.ws == 0) {
@@ -456,8 +524,8 @@ __global__ void __launch_bounds__(kThreads, LG == 8 ? 4 : 3) sddmm_fused(const S
               const int e = j + h + u;
               fresh[u] = !kReuseRows || sr[e] != (e == 0 ? sr[kChunk] : sr[e - 1]);
               if (e < n) {
-                y[u] = seg(rhs_l, sc[e], c);
-                if (fresh[u]) x[u] = seg(lhs_l, sr[e], c);
+                y[u] = seg(rhs_l, sc[e], c, a.cols, kBadColumn);
+                if (fresh[u]) x[u] = seg(lhs_l, sr[e], c, a.rows, kBadRow);
               }
             }
 #pragma unroll
@@ -473,7 +541,7 @@ __global__ void __launch_bounds__(kThreads, LG == 8 ? 4 : 3) sddmm_fused(const S
         const float dot = reduce_batch<LG, BATCH>(p, l, gm);
         const int jl = j + l / kLanesPerElem;
         if (l % kLanesPerElem == 0 && jl < n) {
-          if constexpr (kCsr) a.out_csr[pos[base + jl]] = dot * sv[jl];
+          if constexpr (kCsr) a.out_csr[checked(pos[base + jl], a.nnz, kBadPosition)] = dot * sv[jl];
           else atomicAdd(out + base + jl, dot * sv[jl]);
         }
       }
@@ -488,11 +556,11 @@ __global__ void __launch_bounds__(kThreads, LG == 8 ? 4 : 3) sddmm_fused(const S
   int g = t.group;
   float4 x[FC], x_next[FC];
 #pragma unroll
-  for (int c = 0; c < FC; ++c) x[c] = seg(lhs_l, des[g], c);
+  for (int c = 0; c < FC; ++c) x[c] = seg(lhs_l, des[g], c, a.rows, kBadRow);
   const bool more = g + 1 < groups && (g + 1) * G < t.end;
   if (more) {
 #pragma unroll
-    for (int c = 0; c < FC; ++c) x_next[c] = seg(lhs_l, des[g + 1], c);
+    for (int c = 0; c < FC; ++c) x_next[c] = seg(lhs_l, des[g + 1], c, a.rows, kBadRow);
   }
   for (int base = t.begin; base < t.end; base += kChunk) {
     if (base != t.begin && base % G == 0) {  // the chunk starts group g + 1
@@ -501,7 +569,7 @@ __global__ void __launch_bounds__(kThreads, LG == 8 ? 4 : 3) sddmm_fused(const S
       for (int c = 0; c < FC; ++c) x[c] = x_next[c];
       if (g + 1 < groups && (g + 1) * G < t.end) {
 #pragma unroll
-        for (int c = 0; c < FC; ++c) x_next[c] = seg(lhs_l, des[g + 1], c);
+        for (int c = 0; c < FC; ++c) x_next[c] = seg(lhs_l, des[g + 1], c, a.rows, kBadRow);
       }
     }
 #pragma unroll
@@ -522,7 +590,7 @@ __global__ void __launch_bounds__(kThreads, LG == 8 ? 4 : 3) sddmm_fused(const S
         for (int h = 0; h < BATCH; h += kLoadGroup) {
           float4 y[kLoadGroup];
 #pragma unroll
-          for (int u = 0; u < kLoadGroup; ++u) y[u] = seg(rhs_l, sc[j + h + u], c);
+          for (int u = 0; u < kLoadGroup; ++u) y[u] = seg(rhs_l, sc[j + h + u], c, a.cols, kBadColumn);
 #pragma unroll
           for (int u = 0; u < kLoadGroup; ++u) p[h + u] += dot4(x[c], y[u]);
         }
@@ -530,7 +598,7 @@ __global__ void __launch_bounds__(kThreads, LG == 8 ? 4 : 3) sddmm_fused(const S
       const float dot = reduce_batch<LG, BATCH>(p, l, gm);
       const int jl = j + l / kLanesPerElem;
       if (l % kLanesPerElem == 0) {
-        if constexpr (kCsr) a.out_csr[pos[base + jl]] = dot * sv[jl];
+        if constexpr (kCsr) a.out_csr[checked(pos[base + jl], a.nnz, kBadPosition)] = dot * sv[jl];
         else out[base + jl] = dot * sv[jl];
       }
     }
@@ -541,7 +609,7 @@ __global__ void __launch_bounds__(kThreads, LG == 8 ? 4 : 3) sddmm_fused(const S
 // C[wide_row[slot], :] = float(C + acc[slot, :]) (one rounding), then acc = 0
 // so that the scratch is all-zero for the next call.
 __global__ void __launch_bounds__(256) wide_rows_fold(const int* __restrict__ wide_row, int wide_rows, int N,
-                                                      double* __restrict__ acc, float* __restrict__ C) {
+                                                      double* __restrict__ acc, float* __restrict__ C, int rows) {
   const int per_row = N / 4;
   const long long total = (long long)wide_rows * per_row;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
@@ -549,7 +617,7 @@ __global__ void __launch_bounds__(256) wide_rows_fold(const int* __restrict__ wi
     const long long slot = i / per_row;
     const int q = int(i - slot * per_row);
     double2* a2 = reinterpret_cast<double2*>(acc + slot * N + 4 * q);
-    float4* c4 = reinterpret_cast<float4*>(C + (long long)wide_row[slot] * N + 4 * q);
+    float4* c4 = reinterpret_cast<float4*>(C + checked(wide_row[slot], rows, kBadRow) * N + 4 * q);
     const double2 lo = a2[0], hi = a2[1];
     float4 c = *c4;
     c.x = float(double(c.x) + lo.x);
@@ -565,11 +633,14 @@ __global__ void __launch_bounds__(256) wide_rows_fold(const int* __restrict__ wi
 // In-place softmax over each row's entries of a CSR-order array (one warp per row):
 // v[p] = exp(v[p] - max_row) / sum_row exp(v[q] - max_row).
 __global__ void __launch_bounds__(256) edge_softmax_rows(const int* __restrict__ row_ptr, int rows,
-                                                         float* __restrict__ v) {
+                                                         float* __restrict__ v, int nnz) {
   const int lane = threadIdx.x & 31;
   const int warps = (gridDim.x * blockDim.x) >> 5;
   for (int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < rows; r += warps) {
     const int b = row_ptr[r], e = row_ptr[r + 1];
+    if (!in_range(b, nnz + 1LL, kBadRowPtr) || !in_range(e, nnz + 1LL, kBadRowPtr) ||
+        !in_range(e - b, nnz + 1LL, kBadRowPtr))
+      continue;
     if (b == e) continue;
     float mx = -INFINITY;
     for (int p = b + lane; p < e; p += 32) mx = fmaxf(mx, v[p]);
@@ -599,6 +670,7 @@ WorksetView view_of(const Matrix& m) {
     v.des[s] = m.group_des[s];
     v.group_len[s] = s == 0 ? 0 : group_size(s);
     v.groups[s] = m.group_num[s];
+    v.len[s] = m.ws_size[s];
   }
   return v;
 }
@@ -609,6 +681,11 @@ WorksetView view_of(const Matrix& m) {
 // the matrix has no work.
 template <typename Args>
 bool set_tasks(Args& a, const Matrix& m, int N) {
+  a.S = m.S;
+  a.rows = m.rows;
+  a.cols = m.cols;
+  a.nnz = m.nnz;
+  a.wide_rows = m.wide_rows;
   const int o = (long long)m.cols * N * 4 > m.l2_bytes / 2 ? kSliceOrder : kRowOrder;
   const int r = N < 128 ? kFineResidue : kCoarseResidue;
   a.block_tasks = m.block_tasks[o];
@@ -624,6 +701,26 @@ namespace {
 
 // SpMM with the layout's values (values == nullptr) or with per-call values in CSR
 // order (kValues).
+// Checked build: waits for the launches on `stream` and raises the first index
+// failure the kernels recorded (clearing it).  Nothing in the release build.
+void check_bounds(cudaStream_t stream) {
+  if constexpr (kChecked) {
+    PSB_CUDA(cudaStreamSynchronize(stream));
+    unsigned long long status = 0;
+    PSB_CUDA(cudaMemcpyFromSymbol(&status, g_bounds_status, sizeof(status)));
+    if (status == 0) return;
+    const unsigned long long zero = 0;
+    PSB_CUDA(cudaMemcpyToSymbol(g_bounds_status, &zero, sizeof(zero)));
+    static const char* const what[] = {"", "task outside its workset", "column index out of range",
+                                       "destination row out of range", "group index out of range",
+                                       "CSR position out of range", "row pointer out of range"};
+    const unsigned code = unsigned(status >> 32);
+    throw std::runtime_error(std::string("bounds check failed in an operator kernel: ") +
+                             (code < 7 ? what[code] : "unknown") + " (index " +
+                             std::to_string(int(unsigned(status & 0xffffffffu))) + ")");
+  }
+}
+
 template <bool kValues>
 void spmm_run(const Matrix& m, int N, const float* B, float* C, const float* values, cudaStream_t stream) {
   SpmmArgs a{};
@@ -651,6 +748,7 @@ void spmm_run(const Matrix& m, int N, const float* B, float* C, const float* val
   };
   if (m.wide_rows == 0) {
     launch();
+    check_bounds(stream);
     return;
   }
   // Wide rows: the matrix's FP64 scratch.  Eager calls that share it are
@@ -678,9 +776,10 @@ void spmm_run(const Matrix& m, int N, const float* B, float* C, const float* val
   launch();
   const long long total = (long long)m.wide_rows * (N / 4);
   const unsigned blocks = unsigned(std::min<long long>((total + 255) / 256, 8LL * device_sms()));
-  wide_rows_fold<<<blocks, 256, 0, stream>>>(m.wide_row, m.wide_rows, N, m.wide_acc, C);
+  wide_rows_fold<<<blocks, 256, 0, stream>>>(m.wide_row, m.wide_rows, N, m.wide_acc, C, m.rows);
   PSB_LAUNCH_CHECK();
   if (capture == cudaStreamCaptureStatusNone) PSB_CUDA(cudaEventRecord(m.wide_ready, stream));
+  check_bounds(stream);
 }
 
 }  // namespace
@@ -696,8 +795,9 @@ void spmm_values_launch(const Matrix& m, int N, const float* values, const float
 
 void edge_softmax_launch(const Matrix& m, float* values, cudaStream_t stream) {
   const unsigned blocks = unsigned(std::max<long long>(1, std::min<long long>(((long long)m.rows + 7) / 8, 16LL * device_sms())));
-  edge_softmax_rows<<<blocks, 256, 0, stream>>>(m.row_ptr, m.rows, values);
+  edge_softmax_rows<<<blocks, 256, 0, stream>>>(m.row_ptr, m.rows, values, m.nnz);
   PSB_LAUNCH_CHECK();
+  check_bounds(stream);
 }
 
 void sddmm_launch(const Matrix& m, int N, const float* lhs, const float* rhs, float* const* out,
@@ -715,6 +815,7 @@ void sddmm_launch(const Matrix& m, int N, const float* lhs, const float* rhs, fl
     sddmm_fused<8, 1, 8><<<task_blocks(a.num_tasks, 8), kThreads, 0, stream>>>(a);
   }
   PSB_LAUNCH_CHECK();
+  check_bounds(stream);
 }
 
 void sddmm_csr_launch(const Matrix& m, int N, const float* lhs, const float* rhs, float* out,
@@ -733,6 +834,7 @@ void sddmm_csr_launch(const Matrix& m, int N, const float* lhs, const float* rhs
     sddmm_fused<8, 1, 8, true><<<task_blocks(a.num_tasks, 8), kThreads, 0, stream>>>(a);
   }
   PSB_LAUNCH_CHECK();
+  check_bounds(stream);
 }
 
 // --- SpMM without allocation (ps_spmm_noalloc) -------------------------------
@@ -810,9 +912,10 @@ void spmm_launch_noalloc(const Matrix& m, int N, const float* B, float* C, cudaS
   if (m.wide_rows > 0) {
     const long long total = (long long)m.wide_rows * (N / 4);
     const unsigned blocks = unsigned(std::min<long long>((total + 255) / 256, 8LL * device_sms()));
-    wide_rows_fold<<<blocks, 256, 0, stream>>>(m.wide_row, m.wide_rows, N, a.wide_acc, C);
+    wide_rows_fold<<<blocks, 256, 0, stream>>>(m.wide_row, m.wide_rows, N, a.wide_acc, C, m.rows);
     PSB_LAUNCH_CHECK();
   }
+  check_bounds(stream);
 }
 
 }  // namespace psb

@@ -31,6 +31,14 @@ def test_library_exports_every_declared_symbol():
     assert not missing, missing
 
 
+def test_bounds_checked_library_exports_every_declared_symbol():
+    """The debug build (bounds-checked kernels) is a drop-in for the release library."""
+    path = os.path.join(ROOT, "powersparse_b200", "lib", "libpowersparse_b200_checked.so")
+    lib = ctypes.CDLL(path)
+    missing = [s for s in declared_symbols() if not hasattr(lib, s)]
+    assert not missing, missing
+
+
 def test_python_binding_covers_every_declared_symbol():
     bound = {name for name, _, _ in psb._SIGNATURES}
     assert set(declared_symbols()) <= bound
