@@ -48,10 +48,11 @@ def _worker(rank, port, result_dir, mode):
         outcome["error"] = str(e)
     outcome["seconds"] = time.monotonic() - t0
     try:
-        dist.destroy_process_group()
-    finally:
-        with open(os.path.join(result_dir, f"rank0_{mode}.json"), "w") as f:
-            json.dump(outcome, f)
+        dist.destroy_process_group()  # abort the group; with its peer gone this may itself report an error
+    except Exception as e:  # noqa: BLE001 - recorded, the rank still exits cleanly
+        outcome["destroy_error"] = str(e)[:200]
+    with open(os.path.join(result_dir, f"rank0_{mode}.json"), "w") as f:
+        json.dump(outcome, f)
 
 
 @pytest.mark.parametrize("mode", ["raise", "leave"])
