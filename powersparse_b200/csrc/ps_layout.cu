@@ -254,13 +254,15 @@ __global__ void add_group_lengths(const int* __restrict__ des, int groups, int g
     atomicAdd(&lens[des[g]], res_off ? res_off[g + 1] - res_off[g] : group_len);
 }
 
-__global__ void residue_rows(const int* __restrict__ res_off, const int* __restrict__ des, int groups,
-                             int* __restrict__ row_of) {
+// Row word of every residue element: its group's destination row, with bit 31 set
+// when the group adds atomically (residue_atomic).
+__global__ void residue_rows(const int* __restrict__ res_off, const int* __restrict__ des,
+                             const bool* __restrict__ atomic, int groups, int* __restrict__ row_of) {
   const int lane = threadIdx.x & 31;
   const int warps = (gridDim.x * blockDim.x) >> 5;
   for (int g = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; g < groups; g += warps) {
-    const int r = des[g];
-    for (int e = res_off[g] + lane; e < res_off[g + 1]; e += 32) row_of[e] = r;
+    const int w = int(unsigned(des[g]) | (atomic[g] ? 0x80000000u : 0u));
+    for (int e = res_off[g] + lane; e < res_off[g + 1]; e += 32) row_of[e] = w;
   }
 }
 
@@ -414,7 +416,8 @@ void finish_matrix(Matrix& mat, const std::vector<int>& h_res_off) {
   }
   if (m->ws_size[0] > 0) {
     DeviceArray<int> rows_of(size_t(m->ws_size[0]));
-    residue_rows<<<grid_for(G0, 8, kBlocks), 256, 0, st>>>(m->residue_offset, m->group_des[0], G0, rows_of.get());
+    residue_rows<<<grid_for(G0, 8, kBlocks), 256, 0, st>>>(m->residue_offset, m->group_des[0], m->residue_atomic,
+                                                           G0, rows_of.get());
     PSB_LAUNCH_CHECK();
     m->residue_row = rows_of.release_ownership();
   }

@@ -71,8 +71,10 @@ struct Matrix {
   Task* residue_tasks[2] = {};
   int num_residue_tasks[2] = {};
   long long l2_bytes = 0;              // L2 size of the device (picks the block order)
-  // Destination row of every residue element (residue groups are short, so SDDMM
-  // reads the lhs row per element instead of switching rows at group boundaries).
+  // Row word of every residue element: its group's destination row, bit 31 set when
+  // the group adds atomically (its row has other groups).  Residue groups are short,
+  // so SDDMM reads the lhs row per element and SpMM finds group ends by comparing
+  // neighbouring words, instead of switching through group metadata.
   int* residue_row = nullptr;          // device [ws_size[0]]
 
   // Wide rows: rows split into at least kWideRowSlices block-slice tasks.  SpMM

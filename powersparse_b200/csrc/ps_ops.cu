@@ -39,7 +39,12 @@ constexpr int kThreads = kWarpsPerBlock * 32;
 constexpr int kChunk = 32;        // staged elements per lane group
 constexpr int kUnroll = 4;        // gathers in flight per lane group (residue, SDDMM)
 constexpr int kBlockUnroll = 8;   // gathers in flight per lane group (SpMM block groups)
-static_assert(kChunk % kUnroll == 0 && kChunk % kBlockUnroll == 0, "unrolls must divide the staged chunk");
+// Gathers in flight per lane group on SpMM residue groups: 8 spills at 64 registers
+// and measured 7% slower at N=32 (config 2); 4 keeps the row-word bookkeeping free.
+constexpr int kResidueUnroll = 4;
+static_assert(kChunk % kUnroll == 0 && kChunk % kBlockUnroll == 0 && kChunk % kResidueUnroll == 0 &&
+                  kResidueUnroll % 4 == 0,
+              "unrolls must divide the staged chunk");
 
 struct WorksetView {
   const int* col[kMaxWorksets];
@@ -122,9 +127,7 @@ struct SpmmArgs {
   int num_block;
   const Task* res_tasks;    // tasks [num_block, num_tasks)
   int num_tasks;
-  const int* res_off;
-  const bool* res_atomic;
-  int res_groups;
+  const int* res_row;       // row word of every residue element (Matrix::residue_row)
   const float* B;
   float* C;
   long long ldb;  // N
@@ -172,6 +175,7 @@ __global__ void __launch_bounds__(kThreads, 4) spmm_fused(const SpmmArgs a) {
   __shared__ __align__(16) int s_col[kWarpsPerBlock][NG][kStride];
   __shared__ __align__(16) float s_val[kWarpsPerBlock][NG][kStride];
   __shared__ int2 s_cv[kPairs ? kWarpsPerBlock : 1][kChunk + 1];
+  __shared__ __align__(16) int s_row[kWarpsPerBlock][NG][kStride];  // residue row words (kChunk + 1 used)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q = lane / LG, l = lane % LG;
   const unsigned gm = LG == 32 ? 0xffffffffu : (((1u << LG) - 1u) << (q * LG));
@@ -210,18 +214,13 @@ __global__ void __launch_bounds__(kThreads, 4) spmm_fused(const SpmmArgs a) {
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 
   if (t.ws == 0) {
-    // Residue: groups of <= 31 elements; lane l holds the metadata of group wbase + l.
-    int wbase = t.group;
-    int g_end = 0, g_row = 0, g_atomic = 0;
-    if (wbase + l < a.res_groups) {
-      g_end = a.res_off[wbase + l + 1];
-      g_row = des[wbase + l];
-      g_atomic = a.res_atomic[wbase + l];
-    }
-    int widx = 0;
-    int cur_end = __shfl_sync(gm, g_end, 0, LG);
-    int cur_row = __shfl_sync(gm, g_row, 0, LG);
-    bool cur_atomic = __shfl_sync(gm, g_atomic, 0, LG);
+    // Residue: groups of <= 31 elements.  Every element carries its row word
+    // (destination row | atomic << 31, Matrix::residue_row); a group ends where the
+    // next element's word differs or the task ends, so a boundary costs one shared
+    // compare, and 8 gathers stay in flight as in the block path.  (Consecutive
+    // groups of one row, the fine groups when S == 1, are all atomic and are added
+    // as one sum.)
+    int* sr = s_row[warp][q];
     for (int base = t.begin; base < t.end; base += kChunk) {
       const int n = min(kChunk, t.end - base);
       // Residue tasks start anywhere, so they are staged element by element.
@@ -229,61 +228,39 @@ __global__ void __launch_bounds__(kThreads, 4) spmm_fused(const SpmmArgs a) {
       for (int r = 0; r < kChunk / LG; ++r) {
         const int i = l + r * LG;
         if (i < n) {
-          if constexpr (kPairs) {
-            cv[i] = make_int2(__ldcs(col + base + i), __float_as_int(value1(base + i)));
-          } else {
-            sc[i] = __ldcs(col + base + i);
-            sv[i] = value1(base + i);
-          }
+          sc[i] = __ldcs(col + base + i);
+          sv[i] = value1(base + i);
+          sr[i] = __ldcs(a.res_row + base + i);
         }
       }
+      if (l == 0) sr[n] = base + n < t.end ? __ldcs(a.res_row + base + n) : -1;  // -1: no row has this word
       __syncwarp(gm);
-      for (int j = 0; j < n; j += kUnroll) {
-        int cc[kUnroll];
-        float vv[kUnroll];
-        if constexpr (kPairs) {
+#pragma unroll 1
+      for (int j = 0; j < n; j += kResidueUnroll) {
+        float4 b[kResidueUnroll];
 #pragma unroll
-          for (int u = 0; u < kUnroll; ++u) {
-            const int2 e = cv[j + u];
-            cc[u] = e.x;
-            vv[u] = __int_as_float(e.y);
-          }
-        } else {
-          const int4 c4 = *reinterpret_cast<const int4*>(sc + j);
-          const float4 v4 = *reinterpret_cast<const float4*>(sv + j);
-          cc[0] = c4.x; cc[1] = c4.y; cc[2] = c4.z; cc[3] = c4.w;
-          vv[0] = v4.x; vv[1] = v4.y; vv[2] = v4.z; vv[3] = v4.w;
+        for (int u = 0; u < kResidueUnroll; u += 4) {
+          const int4 c4 = *reinterpret_cast<const int4*>(sc + j + u);
+          if (j + u < n) b[u] = gather(c4.x);
+          if (j + u + 1 < n) b[u + 1] = gather(c4.y);
+          if (j + u + 2 < n) b[u + 2] = gather(c4.z);
+          if (j + u + 3 < n) b[u + 3] = gather(c4.w);
         }
-        float4 b[kUnroll];
 #pragma unroll
-        for (int u = 0; u < kUnroll; ++u)
-          if (j + u < n) b[u] = gather(cc[u]);
-#pragma unroll
-        for (int u = 0; u < kUnroll; ++u) {
+        for (int u = 0; u < kResidueUnroll; ++u) {
           if (j + u < n) {
-            if (base + j + u == cur_end) {
-              if (in_range(cur_row, a.rows, kBadRow)) emit4(Cl + (long long)cur_row * a.ldb, acc, cur_atomic);
+            fma4(acc, sv[j + u], b[u]);
+            const int w = sr[j + u];
+            if (w != sr[j + u + 1]) {
+              const int row = w & 0x7fffffff;
+              if (in_range(row, a.rows, kBadRow)) emit4(Cl + (long long)row * a.ldb, acc, w < 0);
               acc = make_float4(0.f, 0.f, 0.f, 0.f);
-              if (++widx == LG) {
-                wbase += LG;
-                widx = 0;
-                if (wbase + l < a.res_groups) {
-                  g_end = a.res_off[wbase + l + 1];
-                  g_row = des[wbase + l];
-                  g_atomic = a.res_atomic[wbase + l];
-                }
-              }
-              cur_end = __shfl_sync(gm, g_end, widx, LG);
-              cur_row = __shfl_sync(gm, g_row, widx, LG);
-              cur_atomic = __shfl_sync(gm, g_atomic, widx, LG);
             }
-            fma4(acc, vv[u], b[u]);
           }
         }
       }
       __syncwarp(gm);
     }
-    if (in_range(cur_row, a.rows, kBadRow)) emit4(Cl + (long long)cur_row * a.ldb, acc, cur_atomic);
     return;
   }
 
@@ -501,7 +478,7 @@ __global__ void __launch_bounds__(kThreads, LG == 8 ? 4 : 3) sddmm_fused(const S
         if (i < n) {
           sc[i] = __ldcs(col + base + i);
           sv[i] = __ldcs(val + base + i);
-          sr[i] = __ldcs(a.res_row + base + i);
+          sr[i] = __ldcs(a.res_row + base + i) & 0x7fffffff;  // the row (bit 31: SpMM's atomic flag)
         }
       }
       if (l == 0) sr[kChunk] = last_row;
@@ -726,9 +703,7 @@ void spmm_run(const Matrix& m, int N, const float* B, float* C, const float* val
   SpmmArgs a{};
   if (!set_tasks(a, m, N)) return;
   a.ws = view_of(m);
-  a.res_off = m.residue_offset;
-  a.res_atomic = m.residue_atomic;
-  a.res_groups = m.group_num[0];
+  a.res_row = m.residue_row;
   a.B = B;
   a.C = C;
   a.ldb = N;
@@ -890,9 +865,7 @@ void spmm_launch_noalloc(const Matrix& m, int N, const float* B, float* C, cudaS
   SpmmArgs a{};
   if (!set_tasks(a, m, N)) return;
   a.ws = view_of(m);
-  a.res_off = m.residue_offset;
-  a.res_atomic = m.residue_atomic;
-  a.res_groups = m.group_num[0];
+  a.res_row = m.residue_row;
   a.B = B;
   a.C = C;
   a.ldb = N;
