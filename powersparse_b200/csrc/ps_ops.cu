@@ -639,6 +639,17 @@ unsigned task_blocks(int num_tasks, int lane_group) {
   return unsigned((num_tasks + per_block - 1) / per_block);
 }
 
+// Launches sddmm_fused<LG, FC, BATCH, kCsr> for dense rows of N floats.  The kernel
+// addresses rows with its compile-time length 4 * LG * FC, so that must be N: a
+// shape launched at another N would read and write past the operands.
+template <int LG, int FC, int BATCH, bool kCsr>
+void launch_sddmm(const SddmmArgs& a, int N, cudaStream_t stream) {
+  if (N != 4 * LG * FC)
+    throw std::logic_error("SDDMM kernel shape for N=" + std::to_string(4 * LG * FC) + " launched at N=" +
+                           std::to_string(N));
+  sddmm_fused<LG, FC, BATCH, kCsr><<<task_blocks(a.num_tasks, LG), kThreads, 0, stream>>>(a);
+}
+
 WorksetView view_of(const Matrix& m) {
   WorksetView v{};
   for (int s = 0; s < m.S; ++s) {
@@ -785,9 +796,9 @@ void sddmm_launch(const Matrix& m, int N, const float* lhs, const float* rhs, fl
   a.lhs = lhs;
   a.rhs = rhs;
   if (N == 128) {
-    sddmm_fused<16, 2, 4><<<task_blocks(a.num_tasks, 16), kThreads, 0, stream>>>(a);
+    launch_sddmm<16, 2, 4, false>(a, N, stream);
   } else {
-    sddmm_fused<8, 1, 8><<<task_blocks(a.num_tasks, 8), kThreads, 0, stream>>>(a);
+    launch_sddmm<8, 1, 8, false>(a, N, stream);
   }
   PSB_LAUNCH_CHECK();
   check_bounds(stream);
@@ -804,9 +815,9 @@ void sddmm_csr_launch(const Matrix& m, int N, const float* lhs, const float* rhs
   a.lhs = lhs;
   a.rhs = rhs;
   if (N == 128) {
-    sddmm_fused<16, 2, 4, true><<<task_blocks(a.num_tasks, 16), kThreads, 0, stream>>>(a);
+    launch_sddmm<16, 2, 4, true>(a, N, stream);
   } else {
-    sddmm_fused<8, 1, 8, true><<<task_blocks(a.num_tasks, 8), kThreads, 0, stream>>>(a);
+    launch_sddmm<8, 1, 8, true>(a, N, stream);
   }
   PSB_LAUNCH_CHECK();
   check_bounds(stream);
