@@ -226,6 +226,9 @@ def main() -> None:
     ap.add_argument("--workload", choices=["cfg2", "cfg5"], default="cfg2",
                     help="cfg2: config 2 per GPU (weak scaling, default); cfg5: the config-5 R-MAT graph "
                          "(16.8M nodes, ~1B nnz) split over the GPUs (strong scaling)")
+    ap.add_argument("--profile-op", choices=["spmm", "sddmm"], default=None,
+                    help="only build the workload and run this operator at --n, --warmup + --steps times "
+                         "(a small, single-kernel process for profilers); prints one short JSON line")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -250,6 +253,12 @@ def main() -> None:
     N = args.n
     panel, cuts, nnz_total = build_workload(rank, world, device, args.workload)
     m = psb.PowerSparseMatrixGPU(panel.rows, panel.cols, panel.nnz, panel.row_ptr, panel.col_ind, panel.values)
+    if args.profile_op:
+        profile_op(psb, m, panel, args, device)
+        m.close()
+        if dist:
+            dist.destroy_process_group()
+        return
     if rank == 0:
         B = dense_B(panel.cols, N, device)
     else:
@@ -448,6 +457,33 @@ def main() -> None:
     if dist:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def profile_op(psb, m, panel, args, device) -> None:
+    """One operator on the panel, --warmup + --steps calls and nothing else on the
+    device but its operands: the process profilers capture (e.g. ncu -k ... -s W -c 1)."""
+    import torch
+    N = args.n
+    B = dense_B(panel.cols, N, device)
+    if args.profile_op == "spmm":
+        C = torch.zeros((panel.rows, N), dtype=torch.float32, device=device)
+        run = lambda: psb.SpMM(m, N, B, C)
+    else:
+        X = dense_B(panel.rows, N, device, seed=202)
+        outs = [torch.zeros(max(m.workset_size(s), 1), dtype=torch.float32, device=device)
+                for s in range(m.GroupTypeNum())]
+        run = lambda: psb.SDDMM(m, N, X, B, outs)
+    for _ in range(args.warmup):
+        run()
+    torch.cuda.synchronize(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        run()
+    e1.record()
+    torch.cuda.synchronize(device)
+    print(json.dumps({"profile_op": args.profile_op, "N": N, "nnz": panel.nnz, "calls": args.warmup + args.steps,
+                      "ms": round(e0.elapsed_time(e1) / max(args.steps, 1), 4)}), flush=True)
 
 
 def cpu_spmm_rate(panel, B_host: np.ndarray, min_seconds: float, max_passes: int):
