@@ -221,6 +221,8 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--n", type=int, default=128)
     ap.add_argument("--e2e-steps", type=int, default=8)
+    ap.add_argument("--e2e-chunks", type=int, default=4,
+                    help="row chunks (one stream each) per host<->device copy of the e2e pipeline")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-cfg5", action="store_true", help="skip the configuration-5 extra")
     ap.add_argument("--workload", choices=["cfg2", "cfg5"], default="cfg2",
@@ -412,10 +414,10 @@ def main() -> None:
         del full
 
     if world == 1:
-        e2e = e2e_whole(psb, m, panel, B, C, N, device, stream, args.e2e_steps, nnz_total)
+        e2e = e2e_whole(psb, m, panel, B, C, N, device, stream, args.e2e_steps, nnz_total, args.e2e_chunks)
     else:
         e2e = e2e_sharded(psb, m, panel, B, N, rank, world, device, stream, dist, args.e2e_steps, nnz_total,
-                          max_over_ranks)
+                          max_over_ranks, args.e2e_chunks)
 
     cpu = None
     hB = None
@@ -501,47 +503,74 @@ def cpu_spmm_rate(panel, B_host: np.ndarray, min_seconds: float, max_passes: int
     return flops / t / 1e9, threads, passes, t
 
 
-def e2e_whole(psb, m, panel, B, C, N, device, stream, steps, nnz_total) -> dict:
+class _ChunkedCopy:
+    """A host<->device copy of the rows of a tensor, cut into `k` row chunks that
+    copy on `k` streams.  With one stream per direction, concurrent uploads and
+    readbacks each reach ~42 GB/s on the B200 box's PCIe; cut into 4 chunks per
+    direction they reach ~46 GB/s.  `done[j]` holds the chunks' events for buffer
+    set j."""
+
+    def __init__(self, device, k: int):
+        import torch
+        self.streams = [torch.cuda.Stream(device) for _ in range(k)]
+        self.done = [[torch.cuda.Event() for _ in range(k)] for _ in range(2)]
+
+    def run(self, dst, src, j: int, after) -> None:
+        import torch
+        rows, k = src.shape[0], len(self.streams)
+        for c, s in enumerate(self.streams):
+            lo, hi = rows * c // k, rows * (c + 1) // k
+            for e in after:
+                s.wait_event(e)
+            with torch.cuda.stream(s):
+                dst[lo:hi].copy_(src[lo:hi], non_blocking=True)
+            self.done[j][c].record(s)
+
+    def wait(self, stream, j: int) -> None:
+        for e in self.done[j]:
+            stream.wait_event(e)
+
+    def events(self) -> list:
+        return [e for pair in self.done for e in pair]
+
+
+def e2e_whole(psb, m, panel, B, C, N, device, stream, steps, nnz_total, chunks) -> dict:
     """One GPU, end to end through the public API with host buffers: every step copies
     its B in from pinned host memory, zeroes C, runs SpMM and copies C back out; two
-    buffer sets on three streams let step i+1's upload overlap step i's readback
-    (PCIe is full duplex).  Per-step bytes are unchanged by the overlap."""
+    buffer sets let step i+1's upload overlap step i's readback (PCIe is full
+    duplex), each copy cut into `chunks` row chunks on their own streams.  Per-step
+    bytes are unchanged by the overlap."""
     import torch
     hB = B.cpu().pin_memory()
     hC = [torch.empty((panel.rows, N), dtype=torch.float32).pin_memory() for _ in range(2)]
     dB = [torch.empty_like(B) for _ in range(2)]
     dC = [torch.empty_like(C) for _ in range(2)]
-    s_in, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
-    ev = lambda: torch.cuda.Event()
-    in_done, comp_done, out_done = [ev(), ev()], [ev(), ev()], [ev(), ev()]
+    up, down = _ChunkedCopy(device, chunks), _ChunkedCopy(device, chunks)
+    comp_done = [torch.cuda.Event(), torch.cuda.Event()]
 
     def step(i):
         j = i % 2
-        with torch.cuda.stream(s_in):
-            s_in.wait_event(comp_done[j])      # SpMM of step i-2 has read dB[j]
-            dB[j].copy_(hB, non_blocking=True)
-            in_done[j].record(s_in)
-        stream.wait_event(in_done[j])
-        stream.wait_event(out_done[j])         # readback of step i-2 has read dC[j]
+        up.run(dB[j], hB, j, [comp_done[j]])   # after SpMM of step i-2 has read dB[j]
+        up.wait(stream, j)
+        down.wait(stream, j)                   # readback of step i-2 has read dC[j]
         dC[j].zero_()
         psb.SpMM(m, N, dB[j], dC[j], stream)
         comp_done[j].record(stream)
-        with torch.cuda.stream(s_out):
-            s_out.wait_event(comp_done[j])
-            hC[j].copy_(dC[j], non_blocking=True)
-            out_done[j].record(s_out)
+        down.run(hC[j], dC[j], j, [comp_done[j]])
 
-    ms = _run_pipeline(step, [in_done, comp_done, out_done], stream, device, steps, None)
+    ms = _run_pipeline(step, up.events() + down.events() + comp_done, stream, device, steps, None)
     return {"value": round(2.0 * nnz_total * N / (ms * 1e-3) / 1e9, 2), "unit": "GFLOP/s",
             "h2d_bytes_per_step": int(hB.numel() * 4), "d2h_bytes_per_step": int(hC[0].numel() * 4),
-            "ms_per_step": round(ms, 3), "steps": steps}
+            "ms_per_step": round(ms, 3), "steps": steps, "copy_chunks": chunks}
 
 
-def e2e_sharded(psb, m, panel, B, N, rank, world, device, stream, dist, steps, nnz_total, max_over_ranks) -> dict:
+def e2e_sharded(psb, m, panel, B, N, rank, world, device, stream, dist, steps, nnz_total, max_over_ranks,
+                chunks) -> dict:
     """N GPUs, end to end: every rank uploads its 1/N slice of B from pinned host
     memory, the ranks all-gather B over NVLink (NCCL), each runs SpMM on its panel and
     reads back only its own C panel.  Two buffer sets; upload, all-gather, SpMM and
-    readback of consecutive steps overlap on four streams."""
+    readback of consecutive steps overlap, the copies cut into `chunks` row chunks on
+    their own streams."""
     import torch
     cols = B.shape[0]
     per = -(-cols // world)
@@ -553,39 +582,34 @@ def e2e_sharded(psb, m, panel, B, N, rank, world, device, stream, dist, steps, n
     d_full = [torch.empty((per * world, N), dtype=torch.float32, device=device) for _ in range(2)]
     dC = [torch.empty((panel.rows, N), dtype=torch.float32, device=device) for _ in range(2)]
     hC = [torch.empty((panel.rows, N), dtype=torch.float32).pin_memory() for _ in range(2)]
-    s_in, s_comm, s_out = (torch.cuda.Stream(device) for _ in range(3))
-    ev = lambda: torch.cuda.Event()
-    in_done, gathered, comp_done, out_done = ([ev(), ev()] for _ in range(4))
+    s_comm = torch.cuda.Stream(device)
+    up, down = _ChunkedCopy(device, chunks), _ChunkedCopy(device, chunks)
+    gathered, comp_done = ([torch.cuda.Event(), torch.cuda.Event()] for _ in range(2))
 
     def step(i):
         j = i % 2
-        with torch.cuda.stream(s_in):
-            s_in.wait_event(gathered[j])       # the all-gather of step i-2 has read d_slice[j]
-            d_slice[j].copy_(h_slice, non_blocking=True)
-            in_done[j].record(s_in)
+        up.run(d_slice[j], h_slice, j, [gathered[j]])  # after the all-gather of step i-2 has read d_slice[j]
+        up.wait(s_comm, j)
+        s_comm.wait_event(comp_done[j])        # SpMM of step i-2 has read d_full[j]
         with torch.cuda.stream(s_comm):
-            s_comm.wait_event(in_done[j])
-            s_comm.wait_event(comp_done[j])    # SpMM of step i-2 has read d_full[j]
             dist.all_gather_into_tensor(d_full[j], d_slice[j])
-            gathered[j].record(s_comm)
+        gathered[j].record(s_comm)
         stream.wait_event(gathered[j])
-        stream.wait_event(out_done[j])         # readback of step i-2 has read dC[j]
+        down.wait(stream, j)                   # readback of step i-2 has read dC[j]
         dC[j].zero_()
         psb.SpMM(m, N, d_full[j], dC[j], stream)
         comp_done[j].record(stream)
-        with torch.cuda.stream(s_out):
-            s_out.wait_event(comp_done[j])
-            hC[j].copy_(dC[j], non_blocking=True)
-            out_done[j].record(s_out)
+        down.run(hC[j], dC[j], j, [comp_done[j]])
 
-    ms = max_over_ranks(_run_pipeline(step, [in_done, gathered, comp_done, out_done], stream, device, steps, dist))
+    ms = max_over_ranks(_run_pipeline(step, up.events() + down.events() + gathered + comp_done, stream, device,
+                                      steps, dist))
     # Correctness of the assembled operand: the gathered B equals the replicated one.
     same = bool(torch.equal(d_full[(steps - 1) % 2][:cols], B))
     return {"value": round(2.0 * nnz_total * N / (ms * 1e-3) / 1e9, 2), "unit": "GFLOP/s",
             "h2d_bytes_per_step": int(h_slice.numel() * 4), "d2h_bytes_per_step": int(hC[0].numel() * 4),
             "bytes_per": "rank", "h2d_bytes_per_step_all_ranks": int(h_slice.numel() * 4 * world),
             "allgather_bytes_in_per_rank": int((world - 1) * per * N * 4),
-            "gathered_B_matches": same, "ms_per_step": round(ms, 3), "steps": steps}
+            "gathered_B_matches": same, "ms_per_step": round(ms, 3), "steps": steps, "copy_chunks": chunks}
 
 
 def _run_pipeline(step, events, stream, device, steps, dist) -> float:
@@ -594,9 +618,8 @@ def _run_pipeline(step, events, stream, device, steps, dist) -> float:
     e1 = torch.cuda.Event(enable_timing=True)
 
     def drain():
-        for pair in events:
-            for e in pair:
-                stream.wait_event(e)
+        for e in events:
+            stream.wait_event(e)
 
     for i in range(2):
         step(i)

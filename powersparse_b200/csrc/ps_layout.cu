@@ -350,9 +350,9 @@ void validate_csr(int rows, int cols, int nnz, const int* row_ptr, const int* co
 // once and row order is 6% faster.
 // `slot_of[s][g]`: wide-row slot of block group g of workset s (empty: none).
 std::vector<Task> build_block_tasks(const Matrix& m, BlockOrder order, const std::vector<std::vector<int>>& slot_of,
-                                    const std::vector<char>& exact_slot) {
+                                    const std::vector<char>& slot_sum) {
   auto slot = [&](int s, int g) { return slot_of[s].empty() ? -1 : slot_of[s][g]; };
-  auto exact = [&](int s, int g) { const int k = slot(s, g); return k >= 0 && exact_slot[size_t(k)] ? 1 : 0; };
+  auto sum = [&](int s, int g) { const int k = slot(s, g); return k >= 0 ? int(slot_sum[size_t(k)]) : 0; };
   std::vector<Task> tasks;
   for (int s = m.S - 1; s >= 1; --s) {
     const int G = group_size(s);
@@ -360,11 +360,11 @@ std::vector<Task> build_block_tasks(const Matrix& m, BlockOrder order, const std
     if (G >= kTaskElems && order == kRowOrder) {
       for (int g = 0; g < groups; ++g)
         for (int off = 0; off < G; off += kTaskElems)
-          tasks.push_back({s, g * G + off, g * G + std::min(G, off + kTaskElems), g, slot(s, g), exact(s, g)});
+          tasks.push_back({s, g * G + off, g * G + std::min(G, off + kTaskElems), g, slot(s, g), sum(s, g)});
     } else if (G >= kTaskElems) {
       for (int off = 0; off < G; off += kTaskElems)
         for (int g = 0; g < groups; ++g)
-          tasks.push_back({s, g * G + off, g * G + std::min(G, off + kTaskElems), g, slot(s, g), exact(s, g)});
+          tasks.push_back({s, g * G + off, g * G + std::min(G, off + kTaskElems), g, slot(s, g), sum(s, g)});
     } else {
       const int per = kTaskElems / G;
       for (int g = 0; g < groups; g += per) {
@@ -425,7 +425,7 @@ void finish_matrix(Matrix& mat, const std::vector<int>& h_res_off) {
   // Wide rows (kWideRowSlices): block slices per row, counted over the groups of
   // the worksets whose groups are cut into slices; slots in row order.
   std::vector<std::vector<int>> slot_of(S);
-  std::vector<char> exact_slot;  // per wide-row slot: exact FP64 products
+  std::vector<char> slot_sum;  // per wide-row slot: its WideSum
   {
     std::vector<std::vector<int>> h_des(S);
     std::vector<int> slices(size_t(m->rows), 0);
@@ -441,7 +441,7 @@ void finish_matrix(Matrix& mat, const std::vector<int>& h_res_off) {
       if (slices[r] >= kWideRowSlices) {
         slot_of_row[r] = int(h_wide_row.size());
         h_wide_row.push_back(r);
-        exact_slot.push_back(slices[r] >= kExactRowSlices ? 1 : 0);
+        slot_sum.push_back(char(slices[r] >= kExactRowSlices ? kWideExact : kWideQuad));
       }
     }
     m->wide_rows = int(h_wide_row.size());
@@ -463,7 +463,7 @@ void finish_matrix(Matrix& mat, const std::vector<int>& h_res_off) {
     PSB_CUDA(cudaMemcpy(*dst, tasks.data(), sizeof(Task) * tasks.size(), cudaMemcpyHostToDevice));
   };
   for (int o : {kRowOrder, kSliceOrder})
-    upload_tasks(build_block_tasks(*m, BlockOrder(o), slot_of, exact_slot), &m->block_tasks[o],
+    upload_tasks(build_block_tasks(*m, BlockOrder(o), slot_of, slot_sum), &m->block_tasks[o],
                  &m->num_block_tasks[o]);
   upload_tasks(build_residue_tasks(*m, h_res_off, kFineResidueTaskElems), &m->residue_tasks[kFineResidue],
                &m->num_residue_tasks[kFineResidue]);

@@ -19,16 +19,15 @@ inline int group_size(int s) { return 32 << (s - 1); }
 // A unit of SpMM/SDDMM work: elements [begin, end) of workset `ws`, starting in
 // group `group`.  Residue tasks cover whole groups; block tasks cover whole
 // groups, or one slice of a group when the group is longer than a task.
-// `slot` >= 0 marks a slice of a wide row (see Matrix::wide_rows); `exact` marks
-// the slices of the longest wide rows (kExactRowSlices), which sum exact FP64
-// products.
+// `slot` >= 0 marks a slice of a wide row (see Matrix::wide_rows); `sum` is then
+// how the slice sums its products (WideSum, chosen by the row's length).
 struct Task {
   int ws;
   int begin;
   int end;
   int group;
   int slot;
-  int exact;
+  int sum;
 };
 
 // A launch runs the block tasks (largest groups first), then the residue tasks.
@@ -127,12 +126,19 @@ constexpr int kFineResidueTaskElems = 64;
 // k >= 8 (rows of >= 2048 elements, R ~ sqrt(row length)) reaches 1e-5, the
 // absolute tolerance, on outputs whose exact value is near zero.
 constexpr int kWideRowSlices = 8;
-// Wide rows with at least this many block slices (65536 elements) add exact FP64
-// products; shorter wide rows add products in Kahan-compensated FP32.  The FMA
-// rounds each product's addend once (about 2^-24 * |v * b|), and over L products
-// those roundings drift by about sqrt(L) * 2^-24 * 0.2 for values in [0, 1] times
-// operands in [-1, 1]: 1e-6 at 65536 elements, 5e-6 at 667k (the longest row of
-// configuration 5), against the 1e-5 absolute tolerance.
+// Summation of a wide-row slice, by the row's block slices (rows of L products;
+// the tolerance bites at 1e-5 absolute, on outputs whose exact value is near zero):
+//   < kExactRowSlices  kWideQuad: chains of 4 FP32 FMAs, the first starting from the
+//                      compensation, each chain added to the slice sum by a Kahan
+//                      step (1.75 operations per product); what it keeps is each
+//                      chain's own rounding, a drift of order sqrt(L) * 2^-24 * |v * b|;
+//   otherwise          kWideExact: exact FP64 products (an FP32 x FP32 product is
+//                      exact in FP64) summed in FP64.
+// Worst element on the 300 longest and ~900 sampled long rows of configurations 2-5
+// at N = 32 and 128, in units of the tolerance: chains 0.39 (rows of 2048-16383
+// products) and 0.46 (16384-65535); a Kahan step per product 0.26 / 0.52 at 2-4% more
+// time; plain FP32 chunk sums 0.99 / 1.32; exact products 0.14 on rows of >= 65536.
+enum WideSum { kWideQuad = 0, kWideExact = 1 };
 constexpr int kExactRowSlices = 256;
 
 }  // namespace psb

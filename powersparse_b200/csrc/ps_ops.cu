@@ -103,10 +103,12 @@ __device__ __forceinline__ void fma4(float4& acc, float s, const float4& b) {
   acc.w = fmaf(s, b.w, acc.w);
 }
 
-// Kahan step: s + c tracks sum(v * b) with the rounding error of every add kept in
-// c (the product enters exactly through the FMA).
-__device__ __forceinline__ void kahan(float& s, float& c, float v, float b) {
-  const float y = fmaf(v, b, -c);
+// Kahan step over a chain of four products: s + c tracks sum(v[i] * b_i); the chain
+// (FP32 FMAs, starting from -c) is one addend, so the step's three adds cover four
+// products.
+__device__ __forceinline__ void kahan4(float& s, float& c, const float* v, float b0, float b1, float b2,
+                                       float b3) {
+  const float y = fmaf(v[3], b3, fmaf(v[2], b2, fmaf(v[1], b1, fmaf(v[0], b0, -c))));
   const float t = s + y;
   c = (t - s) - y;
   s = t;
@@ -302,10 +304,10 @@ __global__ void __launch_bounds__(kThreads, 4) spmm_fused(const SpmmArgs a) {
         vv[0] = v0.x; vv[1] = v0.y; vv[2] = v0.z; vv[3] = v0.w;
       }
     };
-    if (t.slot >= 0 && t.exact) {
-      // Slices of the longest wide rows (Task::exact) add exact products (an FP32 x
-      // FP32 product is exact in FP64) in FP64.  Four gathers at a time: the FP64
-      // sums hold the registers of the other four.
+    if (t.slot >= 0 && t.sum == kWideExact) {
+      // Slices of the longest wide rows add exact products (an FP32 x FP32 product
+      // is exact in FP64) in FP64.  Four gathers at a time: the FP64 sums hold the
+      // registers of the other four.
 #pragma unroll 1
       for (int j = 0; j < kChunk; j += 4) {
         float4 b[4];
@@ -321,11 +323,12 @@ __global__ void __launch_bounds__(kThreads, 4) spmm_fused(const SpmmArgs a) {
         }
       }
     } else if (t.slot >= 0) {
-      // Other wide-row slices: Kahan-compensated FP32 over the chunk, the sum and its
-      // compensation folded into FP64 separately.  Plain FP32 chunk sums would drift
-      // by about sqrt(chunks) * 2^-24 * |chunk sum| over rows of thousands of
-      // elements, above the 1e-5 absolute tolerance where the exact value is near
-      // zero; rows that are not wide hold at most ~2300 elements and keep them.
+      // Other wide-row slices: chains of four products added by Kahan steps (FP32),
+      // the sum and its compensation folded into FP64 separately.  Plain FP32 chunk
+      // sums would drift by about sqrt(chunks) * 2^-24 * |chunk sum| over rows of
+      // thousands of elements, above the 1e-5 absolute tolerance where the exact
+      // value is near zero; rows that are not wide hold at most ~2300 elements and
+      // keep them.
       float4 ks = make_float4(0.f, 0.f, 0.f, 0.f), kc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 1
       for (int j = 0; j < kChunk; j += kBlockUnroll) {
@@ -334,11 +337,11 @@ __global__ void __launch_bounds__(kThreads, 4) spmm_fused(const SpmmArgs a) {
         load4(j, b, vv);
         load4(j + 4, b + 4, vv + 4);
 #pragma unroll
-        for (int u = 0; u < kBlockUnroll; ++u) {
-          kahan(ks.x, kc.x, vv[u], b[u].x);
-          kahan(ks.y, kc.y, vv[u], b[u].y);
-          kahan(ks.z, kc.z, vv[u], b[u].z);
-          kahan(ks.w, kc.w, vv[u], b[u].w);
+        for (int u = 0; u < kBlockUnroll; u += 4) {
+          kahan4(ks.x, kc.x, vv + u, b[u].x, b[u + 1].x, b[u + 2].x, b[u + 3].x);
+          kahan4(ks.y, kc.y, vv + u, b[u].y, b[u + 1].y, b[u + 2].y, b[u + 3].y);
+          kahan4(ks.z, kc.z, vv + u, b[u].z, b[u + 1].z, b[u + 2].z, b[u + 3].z);
+          kahan4(ks.w, kc.w, vv + u, b[u].w, b[u + 1].w, b[u + 2].w, b[u + 3].w);
         }
       }
       dx += double(ks.x) - double(kc.x);
