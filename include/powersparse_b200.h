@@ -99,7 +99,8 @@ const int* const* ps_matrix_csr_position(const ps_matrix* matrix);
  * SDDMM outputs.  Returns -1 for an invalid s. */
 long long ps_matrix_workset_size(const ps_matrix* matrix, int s);
 
-/* Wall time of the preprocessing in ps_matrix_create, milliseconds. */
+/* Wall time of ps_matrix_create, validation of the CSR included (the scope of the
+ * reference benchmark's preprocess_ms, benchmarks/benchmark.cu:128-134), milliseconds. */
 double ps_matrix_preprocess_ms(const ps_matrix* matrix);
 
 /* CUDA device the matrix lives on. */

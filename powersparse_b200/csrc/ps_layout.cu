@@ -24,10 +24,16 @@
 #include <algorithm>
 #include <chrono>
 #include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <future>
 #include <limits>
 #include <memory>
 #include <numeric>
 #include <stdexcept>
+#include <string>
+#include <thread>
+#include <utility>
 
 namespace psb {
 
@@ -286,29 +292,33 @@ unsigned grid_for(long long work, int per_block, int max_blocks) {
 }
 
 // GenerateSigBit in FFC mode, ffc = 2 (utils/matrix_utils.cu:65-128, mode fixed at :55-60).
-// The column order comes from the same libstdc++ std::sort call on the same
-// input, so columns with equal frequency receive the same bits.
+// The column order comes from the same libstdc++ std::sort (introsort, not stable)
+// on the same input, so columns with equal frequency receive the same bits.  The
+// sort runs over (frequency, column) pairs compared by frequency alone: it makes the
+// same comparisons with the same outcomes, so it moves the pairs exactly as the
+// reference's sort of column ids compared through col_nnz moves the ids, and the
+// keys sit next to the ids instead of behind an indirection.
 void signature_bits(int cols, const std::vector<int>& col_nnz, std::vector<int>& bit, int& len) {
-  std::vector<int> by_freq(cols);
-  std::iota(by_freq.begin(), by_freq.end(), 0);
+  std::vector<std::pair<int, int>> by_freq(cols);  // (col_nnz[c], c)
+  for (int c = 0; c < cols; ++c) by_freq[c] = {col_nnz[c], c};
   std::sort(by_freq.begin(), by_freq.end(),
-            [&col_nnz](const int& a, const int& b) { return col_nnz[a] > col_nnz[b]; });
+            [](const std::pair<int, int>& a, const std::pair<int, int>& b) { return a.first > b.first; });
   bit.assign(cols, 0);
   const int top = std::min(2, cols);
   int next = 0;
   long long budget = 0;
   for (; next < top; ++next) {
-    bit[by_freq[next]] = 0;
-    budget += col_nnz[by_freq[next]];
+    bit[by_freq[next].second] = 0;
+    budget += by_freq[next].first;
   }
   int pos = 1;
   while (next < cols) {
     const int first = next;
     long long run = 0;
     while (next < cols) {
-      run += col_nnz[by_freq[next]];
+      run += by_freq[next].first;
       if (run < budget || next == first) {
-        bit[by_freq[next]] = pos;
+        bit[by_freq[next].second] = pos;
         ++next;
       } else {
         break;
@@ -323,18 +333,40 @@ void signature_bits(int cols, const std::vector<int>& col_nnz, std::vector<int>&
   for (int c = 0; c < cols; ++c) bit[c] = std::min(bit[c], len - 1);
 }
 
+// True if any_in(begin, end) is true for a part of [0, n); the parts run on up to
+// hardware_concurrency host threads (one call below 2^20 items per thread).
+template <typename F>
+bool parallel_any(long long n, const F& any_in) {
+  const long long threads =
+      std::min<long long>(std::max(1u, std::thread::hardware_concurrency()), std::max(1LL, n >> 20));
+  if (threads <= 1) return any_in(0LL, n);
+  std::vector<char> hit(size_t(threads), 0);
+  std::vector<std::thread> pool;
+  for (long long t = 0; t < threads; ++t)
+    pool.emplace_back([&, t] { hit[size_t(t)] = any_in(n * t / threads, n * (t + 1) / threads) ? 1 : 0; });
+  for (auto& th : pool) th.join();
+  return std::find(hit.begin(), hit.end(), 1) != hit.end();
+}
+
 void validate_csr(int rows, int cols, int nnz, const int* row_ptr, const int* col_ind, const float* vals) {
-  // Same checks and messages as utils/matrix_utils.cu:475-488.
+  // Same checks, order and messages as utils/matrix_utils.cu:475-488 (each message
+  // names a class of error, not a position, so the scans may run in parallel).
   if (rows <= 0 || cols <= 0 || nnz <= 0 || rows > std::numeric_limits<int>::max() - 32 ||
       nnz > std::numeric_limits<int>::max() - 32 || !row_ptr || !col_ind || !vals)
     throw std::invalid_argument("Expected a nonempty CSR matrix with 32-bit indices");
   if (row_ptr[0] != 0 || row_ptr[rows] != nnz) throw std::invalid_argument("Invalid CSR row-pointer endpoints");
-  for (int r = 0; r < rows; ++r)
-    if (row_ptr[r] < 0 || row_ptr[r] > row_ptr[r + 1])
-      throw std::invalid_argument("CSR row pointers must be nondecreasing");
-  for (int p = 0; p < nnz; ++p)
-    if (col_ind[p] < 0 || col_ind[p] >= cols || !std::isfinite(vals[p]))
-      throw std::invalid_argument("Invalid CSR column index or sparse value");
+  if (parallel_any(rows, [&](long long b, long long e) {
+        for (long long r = b; r < e; ++r)
+          if (row_ptr[r] < 0 || row_ptr[r] > row_ptr[r + 1]) return true;
+        return false;
+      }))
+    throw std::invalid_argument("CSR row pointers must be nondecreasing");
+  if (parallel_any(nnz, [&](long long b, long long e) {
+        for (long long p = b; p < e; ++p)
+          if (col_ind[p] < 0 || col_ind[p] >= cols || !std::isfinite(vals[p])) return true;
+        return false;
+      }))
+    throw std::invalid_argument("Invalid CSR column index or sparse value");
 }
 
 // Block tasks of about kTaskElems elements, largest group sizes first (the
@@ -476,10 +508,39 @@ void finish_matrix(Matrix& mat, const std::vector<int>& h_res_off) {
   PSB_CUDA(cudaDeviceSynchronize());
 }
 
+// Phases of build_matrix.  With the environment variable PSB_PREPROCESS_TRACE set,
+// every phase ends with a device synchronization and the wall time of each phase
+// is printed to stderr on one line when the build ends; otherwise it does nothing.
+class PhaseTrace {
+ public:
+  PhaseTrace() : on_(std::getenv("PSB_PREPROCESS_TRACE") != nullptr), last_(std::chrono::steady_clock::now()) {}
+  ~PhaseTrace() {
+    if (on_) std::fprintf(stderr, "psb preprocess:%s\n", line_.c_str());
+  }
+  void mark(const char* phase) {
+    if (!on_) return;
+    cudaDeviceSynchronize();
+    const auto now = std::chrono::steady_clock::now();
+    char buf[96];
+    std::snprintf(buf, sizeof(buf), " %s=%.1f", phase, std::chrono::duration<double, std::milli>(now - last_).count());
+    line_ += buf;
+    last_ = now;
+  }
+
+ private:
+  bool on_;
+  std::chrono::steady_clock::time_point last_;
+  std::string line_;
+};
+
 Matrix* build_matrix(int rows, int cols, int nnz, const int* row_ptr, const int* col_ind,
                      const float* sp_data, int sm_count) {
-  validate_csr(rows, cols, nnz, row_ptr, col_ind, sp_data);
+  // The time covers the whole constructor, validation included, as the reference's
+  // benchmark times it (benchmarks/benchmark.cu:128-134).
   const auto t0 = std::chrono::steady_clock::now();
+  PhaseTrace trace;
+  validate_csr(rows, cols, nnz, row_ptr, col_ind, sp_data);
+  trace.mark("validate");
   std::unique_ptr<Matrix> m(new Matrix());
   m->rows = rows;
   m->cols = cols;
@@ -495,6 +556,7 @@ Matrix* build_matrix(int rows, int cols, int nnz, const int* row_ptr, const int*
   PSB_CUDA(cudaMemcpyAsync(d_row_ptr.get(), row_ptr, sizeof(int) * (size_t(rows) + 1), cudaMemcpyHostToDevice, st));
   PSB_CUDA(cudaMemcpyAsync(d_col.get(), col_ind, sizeof(int) * size_t(nnz), cudaMemcpyHostToDevice, st));
   PSB_CUDA(cudaMemcpyAsync(d_val.get(), sp_data, sizeof(float) * size_t(nnz), cudaMemcpyHostToDevice, st));
+  trace.mark("upload");
 
   // --- Number of worksets (AnalyzeMatrix).
   {
@@ -515,6 +577,7 @@ Matrix* build_matrix(int rows, int cols, int nnz, const int* row_ptr, const int*
     m->S = S;
   }
   const int S = m->S, fine = m->fine;
+  trace.mark("worksets");
 
   // --- Column frequencies.
   DeviceArray<int> d_col_nnz(cols);
@@ -524,6 +587,13 @@ Matrix* build_matrix(int rows, int cols, int nnz, const int* row_ptr, const int*
   std::vector<int> h_col_nnz(cols);
   PSB_CUDA(cudaMemcpy(h_col_nnz.data(), d_col_nnz.get(), sizeof(int) * size_t(cols), cudaMemcpyDeviceToHost));
   const int maxcnt = *std::max_element(h_col_nnz.begin(), h_col_nnz.end());
+  // GenerateSigBit needs only the column frequencies: its host sort runs on another
+  // thread while the device sorts the rows and builds the groups.
+  std::vector<int> h_sigbit;
+  int signature_len = 0;
+  std::future<void> sig_job =
+      std::async(std::launch::async, [&] { signature_bits(cols, h_col_nnz, h_sigbit, signature_len); });
+  trace.mark("col_freq");
 
   // --- Within-row order: frequency descending, stable (thrust::sort of NNZPoint).
   DeviceArray<uint32_t> perm;  // perm[i] = CSR position of the i-th element in frequency order
@@ -541,6 +611,7 @@ Matrix* build_matrix(int rows, int cols, int nnz, const int* row_ptr, const int*
     perm = alt ? std::move(vals_alt) : std::move(vals);
   }
   d_col_nnz.release();
+  trace.mark("freq_sort");
 
   // --- Groups per workset and their source metadata.
   DeviceArray<int> counts(size_t(S) * rows), prefix(size_t(S) * (size_t(rows) + 1));
@@ -568,10 +639,12 @@ Matrix* build_matrix(int rows, int cols, int nnz, const int* row_ptr, const int*
   group_metadata<<<grid_for(rows, 256, kBlocks), 256, 0, st>>>(d_row_ptr.get(), rows, S, fine, prefix.get(), wa,
                                                                res_size.get(), res_atomic_src.get());
   PSB_LAUNCH_CHECK();
+  trace.mark("groups");
 
   // --- Signatures (GenerateSigBit on the host, bits on the device).
-  std::vector<int> h_sigbit;
-  signature_bits(cols, h_col_nnz, h_sigbit, m->signature_len);
+  sig_job.get();
+  m->signature_len = signature_len;
+  trace.mark("sig_bits_wait");
   const int words = m->signature_len / 32;
   DeviceArray<int> d_sigbit(cols);
   PSB_CUDA(cudaMemcpy(d_sigbit.get(), h_sigbit.data(), sizeof(int) * size_t(cols), cudaMemcpyHostToDevice));
@@ -587,6 +660,7 @@ Matrix* build_matrix(int rows, int cols, int nnz, const int* row_ptr, const int*
   PSB_LAUNCH_CHECK();
   prefix.release();
   d_sigbit.release();
+  trace.mark("signatures");
 
   // --- Signature order of the groups of every workset: stable, lexicographically
   // descending over words (LSD: last word first, as utils/matrix_utils.cu:590-592).
@@ -610,6 +684,7 @@ Matrix* build_matrix(int rows, int cols, int nnz, const int* row_ptr, const int*
       PSB_CUDA(cudaMemcpy(order[s].get(), idx, sizeof(uint32_t) * size_t(G), cudaMemcpyDeviceToDevice));
     sig[s].release();
   }
+  trace.mark("sig_sort");
 
   // --- Final worksets.
   m->col_ind.assign(S, nullptr);
@@ -635,6 +710,7 @@ Matrix* build_matrix(int rows, int cols, int nnz, const int* row_ptr, const int*
   }
   std::vector<int> h_res_off(size_t(G0) + 1);
   PSB_CUDA(cudaMemcpy(h_res_off.data(), res_off.get(), sizeof(int) * (size_t(G0) + 1), cudaMemcpyDeviceToHost));
+  trace.mark("residue_meta");
   const int wcol = bits_for(unsigned(cols - 1));
   for (int s = 0; s < S; ++s) {
     const int G = m->group_num[s];
@@ -671,7 +747,9 @@ Matrix* build_matrix(int rows, int cols, int nnz, const int* row_ptr, const int*
   }
   m->residue_offset = res_off.release_ownership();
   m->row_ptr = d_row_ptr.release_ownership();
+  trace.mark("col_sort");
   finish_matrix(*m, h_res_off);
+  trace.mark("tasks");
   m->preprocess_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
   return m.release();
 }
