@@ -221,7 +221,7 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--n", type=int, default=128)
     ap.add_argument("--e2e-steps", type=int, default=8)
-    ap.add_argument("--e2e-chunks", type=int, default=4,
+    ap.add_argument("--e2e-chunks", type=int, default=1,
                     help="row chunks (one stream each) per host<->device copy of the e2e pipeline")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-cfg5", action="store_true", help="skip the configuration-5 extra")
@@ -505,10 +505,9 @@ def cpu_spmm_rate(panel, B_host: np.ndarray, min_seconds: float, max_passes: int
 
 class _ChunkedCopy:
     """A host<->device copy of the rows of a tensor, cut into `k` row chunks that
-    copy on `k` streams.  With one stream per direction, concurrent uploads and
-    readbacks each reach ~42 GB/s on the B200 box's PCIe; cut into 4 chunks per
-    direction they reach ~46 GB/s.  `done[j]` holds the chunks' events for buffer
-    set j."""
+    copy on `k` streams (`done[j]`: the chunks' events for buffer set j).  Measured
+    in the config-2 e2e pipeline (1.25 GB each way per step): 28.4 ms per step with
+    one chunk, 29.1 with 2, 29.8 with 4, 30.0 with 8, so the default is one."""
 
     def __init__(self, device, k: int):
         import torch
