@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 
 #include <atomic>
+#include <mutex>
 #include <cstdint>
 #include <stdexcept>
 #include <string>
@@ -82,6 +83,63 @@ struct DeviceArray {
     count = 0;
   }
   T* release_ownership() { T* p = ptr; ptr = nullptr; count = 0; return p; }
+  T* get() const { return ptr; }
+};
+
+// The library's stream-ordered memory pool on `device`, for the scratch of the
+// preprocessing.  Its release threshold is unlimited, so memory given back stays
+// mapped for the next allocation (the row sort's buffers become the column sort's)
+// instead of being returned at every synchronization; trim_scratch_pool hands it
+// back to the device when a build ends.
+inline cudaMemPool_t scratch_pool(int device) {
+  static std::mutex mu;
+  static cudaMemPool_t pools[64] = {};
+  if (device < 0 || device >= 64) throw std::invalid_argument("device ordinal out of range");
+  std::lock_guard<std::mutex> lock(mu);
+  if (!pools[device]) {
+    cudaMemPoolProps props = {};
+    props.allocType = cudaMemAllocationTypePinned;
+    props.location.type = cudaMemLocationTypeDevice;
+    props.location.id = device;
+    cudaMemPool_t pool = nullptr;
+    PSB_CUDA(cudaMemPoolCreate(&pool, &props));
+    unsigned long long keep = ~0ULL;
+    PSB_CUDA(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep));
+    pools[device] = pool;
+  }
+  return pools[device];
+}
+
+// Returns the unused memory of the current device's scratch pool after waiting for
+// the device (memory freed in stream order is unused only once the free has run).
+inline void trim_scratch_pool() noexcept {
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess) return;
+  cudaDeviceSynchronize();
+  try {
+    cudaMemPoolTrimTo(scratch_pool(device), 0);
+  } catch (...) {
+  }
+}
+
+// A device buffer in stream order: taken from the scratch pool on `stream` and given
+// back with cudaFreeAsync on the same stream at scope exit, so work already queued
+// on that stream may still use it and neither step waits for the device.
+template <typename T>
+struct StreamArray {
+  T* ptr = nullptr;
+  cudaStream_t stream = nullptr;
+  StreamArray(size_t n, cudaStream_t s) : stream(s) {
+    if (!n) return;
+    int device = 0;
+    PSB_CUDA(cudaGetDevice(&device));
+    PSB_CUDA(cudaMallocFromPoolAsync(reinterpret_cast<void**>(&ptr), n * sizeof(T), scratch_pool(device), s));
+  }
+  StreamArray(const StreamArray&) = delete;
+  StreamArray& operator=(const StreamArray&) = delete;
+  ~StreamArray() {
+    if (ptr) cudaFreeAsync(ptr, stream);
+  }
   T* get() const { return ptr; }
 };
 

@@ -26,9 +26,11 @@
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
+#include <cstring>
 #include <future>
 #include <limits>
 #include <memory>
+#include <mutex>
 #include <numeric>
 #include <stdexcept>
 #include <string>
@@ -206,8 +208,14 @@ __global__ void group_signatures(const int* __restrict__ row_ptr, int rows, int 
   }
 }
 
-__global__ void signature_word_keys(const uint32_t* __restrict__ sig_word, const uint32_t* __restrict__ idx,
-                                    int n, uint32_t* __restrict__ keys) {
+// Keys of one signature word in the current group order.  The order and the keys
+// live in whichever buffer pair *side names (the sort's device-side record).
+__global__ void signature_word_keys(const uint32_t* __restrict__ sig_word, const uint32_t* __restrict__ idx0,
+                                    const uint32_t* __restrict__ idx1, const int* __restrict__ side, int n,
+                                    uint32_t* __restrict__ keys0, uint32_t* __restrict__ keys1) {
+  const bool alt = *side != 0;
+  const uint32_t* __restrict__ idx = alt ? idx1 : idx0;
+  uint32_t* __restrict__ keys = alt ? keys1 : keys0;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
     keys[i] = ~sig_word[idx[i]];  // ascending complement = descending word
 }
@@ -272,10 +280,15 @@ __global__ void residue_rows(const int* __restrict__ res_off, const int* __restr
   }
 }
 
-__global__ void finalize_workset(const uint64_t* __restrict__ keys, const uint32_t* __restrict__ vals,
-                                 long long n, uint64_t col_mask, const float* __restrict__ sp_data,
-                                 int* __restrict__ col_out, float* __restrict__ val_out,
-                                 int* __restrict__ pos_out) {
+// The sorted (key, CSR position) pairs are in whichever buffer pair *side names.
+__global__ void finalize_workset(const uint64_t* __restrict__ keys0, const uint32_t* __restrict__ vals0,
+                                 const uint64_t* __restrict__ keys1, const uint32_t* __restrict__ vals1,
+                                 const int* __restrict__ side, long long n, uint64_t col_mask,
+                                 const float* __restrict__ sp_data, int* __restrict__ col_out,
+                                 float* __restrict__ val_out, int* __restrict__ pos_out) {
+  const bool alt = *side != 0;
+  const uint64_t* __restrict__ keys = alt ? keys1 : keys0;
+  const uint32_t* __restrict__ vals = alt ? vals1 : vals0;
   for (long long q = blockIdx.x * (long long)blockDim.x + threadIdx.x; q < n;
        q += (long long)gridDim.x * blockDim.x) {
     col_out[q] = int(keys[q] & col_mask);
@@ -348,6 +361,94 @@ bool parallel_any(long long n, const F& any_in) {
   return std::find(hit.begin(), hit.end(), 1) != hit.end();
 }
 
+struct HostCopy {
+  void* dst;        // device
+  const void* src;  // pageable host
+  size_t bytes;
+};
+
+// Synchronous host-to-device copy of pageable host arrays.  A pageable cudaMemcpy
+// goes through the driver's staging at ~11 GB/s on the B200 box; here up to 16 host
+// threads each copy 4 MiB pieces into a pinned buffer of their own and start the
+// transfer from it on a stream of their own, so host copies and transfers of
+// different pieces overlap (config 5's 8.2 GB: 730 -> ~300 ms).  Taking pinned
+// memory is slow (with the buffers taken per call, config 2's 0.5 GB took 135-210 ms
+// against 48 ms pageable), so the buffers are taken once, on the first staged upload
+// of the process, and kept until it exits (64 MiB of host memory), and inputs below
+// 1 GiB in total use the plain copy.
+struct PinnedPool {
+  std::mutex mu;  // one staged upload at a time
+  std::vector<void*> bufs;
+};
+PinnedPool& pinned_pool() {
+  static PinnedPool* pool = new PinnedPool();  // never destroyed: CUDA may be gone at exit
+  return *pool;
+}
+
+void upload_pageable(const std::vector<HostCopy>& copies, cudaStream_t st) {
+  size_t total = 0;
+  for (const auto& c : copies) total += c.bytes;
+  if (total < (size_t(1) << 30)) {
+    for (const auto& c : copies)
+      if (c.bytes) PSB_CUDA(cudaMemcpyAsync(c.dst, c.src, c.bytes, cudaMemcpyHostToDevice, st));
+    PSB_CUDA(cudaStreamSynchronize(st));
+    return;
+  }
+  constexpr size_t kPiece = size_t(4) << 20;
+  struct Piece {
+    char* dst;
+    const char* src;
+    size_t bytes;
+  };
+  std::vector<Piece> pieces;
+  for (const auto& c : copies)
+    for (size_t off = 0; off < c.bytes; off += kPiece)
+      pieces.push_back({static_cast<char*>(c.dst) + off, static_cast<const char*>(c.src) + off,
+                        std::min(kPiece, c.bytes - off)});
+  const int threads = int(std::min<size_t>({size_t(16), std::max<size_t>(1, std::thread::hardware_concurrency()),
+                                            pieces.size()}));
+  int device = 0;
+  PSB_CUDA(cudaGetDevice(&device));
+  PSB_CUDA(cudaStreamSynchronize(st));  // the destinations are ready
+  PinnedPool& pool = pinned_pool();
+  std::lock_guard<std::mutex> lock(pool.mu);
+  while (pool.bufs.size() < size_t(threads)) {
+    void* p = nullptr;
+    PSB_CUDA(cudaHostAlloc(&p, kPiece, cudaHostAllocPortable));
+    pool.bufs.push_back(p);
+  }
+  std::vector<std::string> errors(static_cast<size_t>(threads));
+  auto worker = [&](int t) {
+    void* pin = pool.bufs[size_t(t)];
+    cudaStream_t s = nullptr;
+    cudaEvent_t done = nullptr;
+    try {
+      PSB_CUDA(cudaSetDevice(device));  // a new thread starts on device 0
+      PSB_CUDA(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+      PSB_CUDA(cudaEventCreateWithFlags(&done, cudaEventDisableTiming));
+      bool pending = false;
+      for (size_t i = size_t(t); i < pieces.size(); i += size_t(threads)) {
+        if (pending) PSB_CUDA(cudaEventSynchronize(done));  // the pinned buffer is free again
+        std::memcpy(pin, pieces[i].src, pieces[i].bytes);
+        PSB_CUDA(cudaMemcpyAsync(pieces[i].dst, pin, pieces[i].bytes, cudaMemcpyHostToDevice, s));
+        PSB_CUDA(cudaEventRecord(done, s));
+        pending = true;
+      }
+      PSB_CUDA(cudaStreamSynchronize(s));
+    } catch (const std::exception& e) {
+      errors[size_t(t)] = e.what();
+      if (s) cudaStreamSynchronize(s);
+    }
+    if (done) cudaEventDestroy(done);
+    if (s) cudaStreamDestroy(s);
+  };
+  std::vector<std::thread> team;
+  for (int t = 0; t < threads; ++t) team.emplace_back(worker, t);
+  for (auto& th : team) th.join();
+  for (const auto& e : errors)
+    if (!e.empty()) throw CudaError(cudaErrorUnknown, "staged upload: " + e);
+}
+
 void validate_csr(int rows, int cols, int nnz, const int* row_ptr, const int* col_ind, const float* vals) {
   // Same checks, order and messages as utils/matrix_utils.cu:475-488 (each message
   // names a class of error, not a position, so the scans may run in parallel).
@@ -386,6 +487,13 @@ std::vector<Task> build_block_tasks(const Matrix& m, BlockOrder order, const std
   auto slot = [&](int s, int g) { return slot_of[s].empty() ? -1 : slot_of[s][g]; };
   auto sum = [&](int s, int g) { const int k = slot(s, g); return k >= 0 ? int(slot_sum[size_t(k)]) : 0; };
   std::vector<Task> tasks;
+  size_t count = 0;
+  for (int s = 1; s < m.S; ++s) {
+    const int G = group_size(s);
+    count += G >= kTaskElems ? size_t(m.group_num[s]) * size_t(G / kTaskElems)
+                             : size_t(ceil_div(m.group_num[s], kTaskElems / G));
+  }
+  tasks.reserve(count);
   for (int s = m.S - 1; s >= 1; --s) {
     const int G = group_size(s);
     const int groups = m.group_num[s];
@@ -414,6 +522,7 @@ std::vector<Task> build_block_tasks(const Matrix& m, BlockOrder order, const std
 std::vector<Task> build_residue_tasks(const Matrix& m, const std::vector<int>& h_res_off, int elems) {
   std::vector<Task> tasks;
   const int G0 = m.group_num[0];
+  tasks.reserve(std::min<size_t>(size_t(G0), size_t(h_res_off[G0]) / size_t(elems) * 2 + 16));
   int g = 0;
   while (g < G0) {
     const int first = g;
@@ -488,25 +597,81 @@ void finish_matrix(Matrix& mat, const std::vector<int>& h_res_off) {
       PSB_CUDA(cudaEventCreateWithFlags(&m->wide_ready, cudaEventDisableTiming));
     }
   }
+  // The four task lists are independent: built on host threads, uploaded in turn.
   auto upload_tasks = [](const std::vector<Task>& tasks, Task** dst, int* count) {
     *count = int(tasks.size());
     if (tasks.empty()) return;
     PSB_CUDA(cudaMalloc(reinterpret_cast<void**>(dst), sizeof(Task) * tasks.size()));
     PSB_CUDA(cudaMemcpy(*dst, tasks.data(), sizeof(Task) * tasks.size(), cudaMemcpyHostToDevice));
   };
-  for (int o : {kRowOrder, kSliceOrder})
-    upload_tasks(build_block_tasks(*m, BlockOrder(o), slot_of, slot_sum), &m->block_tasks[o],
-                 &m->num_block_tasks[o]);
-  upload_tasks(build_residue_tasks(*m, h_res_off, kFineResidueTaskElems), &m->residue_tasks[kFineResidue],
-               &m->num_residue_tasks[kFineResidue]);
-  upload_tasks(build_residue_tasks(*m, h_res_off, kTaskElems), &m->residue_tasks[kCoarseResidue],
-               &m->num_residue_tasks[kCoarseResidue]);
+  auto row_order = std::async(std::launch::async,
+                              [&] { return build_block_tasks(*m, kRowOrder, slot_of, slot_sum); });
+  auto slice_order = std::async(std::launch::async,
+                                [&] { return build_block_tasks(*m, kSliceOrder, slot_of, slot_sum); });
+  auto fine = std::async(std::launch::async,
+                         [&] { return build_residue_tasks(*m, h_res_off, kFineResidueTaskElems); });
+  const std::vector<Task> coarse = build_residue_tasks(*m, h_res_off, kTaskElems);
+  upload_tasks(row_order.get(), &m->block_tasks[kRowOrder], &m->num_block_tasks[kRowOrder]);
+  upload_tasks(slice_order.get(), &m->block_tasks[kSliceOrder], &m->num_block_tasks[kSliceOrder]);
+  upload_tasks(fine.get(), &m->residue_tasks[kFineResidue], &m->num_residue_tasks[kFineResidue]);
+  upload_tasks(coarse, &m->residue_tasks[kCoarseResidue], &m->num_residue_tasks[kCoarseResidue]);
   int l2 = 0;
   PSB_CUDA(cudaDeviceGetAttribute(&l2, cudaDevAttrL2CacheSize, m->device));
   m->l2_bytes = l2;
   noalloc_prepare(m->device);
   PSB_CUDA(cudaDeviceSynchronize());
+  trim_scratch_pool();
 }
+
+// Non-blocking streams that start after the work queued so far on `parent`;
+// join() makes `parent` wait for everything queued on them (the destructor joins
+// too, if join() was not reached, and then destroys the streams).
+class StreamSet {
+ public:
+  StreamSet(int n, cudaStream_t parent) : parent_(parent), streams_(size_t(n), nullptr) {
+    cudaEvent_t start = nullptr;
+    PSB_CUDA(cudaEventCreateWithFlags(&start, cudaEventDisableTiming));
+    EventGuard g{start};
+    PSB_CUDA(cudaEventRecord(start, parent_));
+    for (auto& s : streams_) {
+      PSB_CUDA(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+      PSB_CUDA(cudaStreamWaitEvent(s, start, 0));
+    }
+  }
+  StreamSet(const StreamSet&) = delete;
+  StreamSet& operator=(const StreamSet&) = delete;
+  ~StreamSet() {
+    if (!joined_) {
+      try {
+        join();
+      } catch (...) {
+      }
+    }
+    for (auto s : streams_)
+      if (s) cudaStreamDestroy(s);
+  }
+  cudaStream_t operator[](int i) const { return streams_[size_t(i)]; }
+  void join() {
+    joined_ = true;
+    for (auto s : streams_) {
+      if (!s) continue;
+      cudaEvent_t done = nullptr;
+      PSB_CUDA(cudaEventCreateWithFlags(&done, cudaEventDisableTiming));
+      EventGuard g{done};
+      PSB_CUDA(cudaEventRecord(done, s));
+      PSB_CUDA(cudaStreamWaitEvent(parent_, done, 0));
+    }
+  }
+
+ private:
+  struct EventGuard {
+    cudaEvent_t e;
+    ~EventGuard() { cudaEventDestroy(e); }
+  };
+  cudaStream_t parent_;
+  std::vector<cudaStream_t> streams_;
+  bool joined_ = false;
+};
 
 // Phases of build_matrix.  With the environment variable PSB_PREPROCESS_TRACE set,
 // every phase ends with a device synchronization and the wall time of each phase
@@ -539,6 +704,9 @@ Matrix* build_matrix(int rows, int cols, int nnz, const int* row_ptr, const int*
   // benchmark times it (benchmarks/benchmark.cu:128-134).
   const auto t0 = std::chrono::steady_clock::now();
   PhaseTrace trace;
+  struct TrimOnExit {
+    ~TrimOnExit() { trim_scratch_pool(); }
+  } trim_on_exit;  // declared before every StreamArray, so it runs after their frees
   validate_csr(rows, cols, nnz, row_ptr, col_ind, sp_data);
   trace.mark("validate");
   std::unique_ptr<Matrix> m(new Matrix());
@@ -553,9 +721,10 @@ Matrix* build_matrix(int rows, int cols, int nnz, const int* row_ptr, const int*
 
   DeviceArray<int> d_row_ptr(size_t(rows) + 1), d_col(nnz);
   DeviceArray<float> d_val(nnz);
-  PSB_CUDA(cudaMemcpyAsync(d_row_ptr.get(), row_ptr, sizeof(int) * (size_t(rows) + 1), cudaMemcpyHostToDevice, st));
-  PSB_CUDA(cudaMemcpyAsync(d_col.get(), col_ind, sizeof(int) * size_t(nnz), cudaMemcpyHostToDevice, st));
-  PSB_CUDA(cudaMemcpyAsync(d_val.get(), sp_data, sizeof(float) * size_t(nnz), cudaMemcpyHostToDevice, st));
+  upload_pageable({{d_row_ptr.get(), row_ptr, sizeof(int) * (size_t(rows) + 1)},
+                   {d_col.get(), col_ind, sizeof(int) * size_t(nnz)},
+                   {d_val.get(), sp_data, sizeof(float) * size_t(nnz)}},
+                  st);
   trace.mark("upload");
 
   // --- Number of worksets (AnalyzeMatrix).
@@ -596,19 +765,21 @@ Matrix* build_matrix(int rows, int cols, int nnz, const int* row_ptr, const int*
   trace.mark("col_freq");
 
   // --- Within-row order: frequency descending, stable (thrust::sort of NNZPoint).
-  DeviceArray<uint32_t> perm;  // perm[i] = CSR position of the i-th element in frequency order
+  // perm[i] = CSR position of the i-th element in frequency order; it lives in one of
+  // the two value buffers of the sort (both stay until the column sorts are done).
+  StreamArray<uint32_t> perm_a(nnz, st), perm_b(nnz, st);
+  uint32_t* perm = nullptr;
   {
-    DeviceArray<uint64_t> keys(nnz), keys_alt(nnz);
-    DeviceArray<uint32_t> vals(nnz), vals_alt(nnz);
+    StreamArray<uint64_t> keys(nnz, st), keys_alt(nnz, st);
     const int wc = bits_for(unsigned(maxcnt));
     const int wr = bits_for(unsigned(rows - 1));
     freq_sort_keys<<<grid_for(rows, 8, kBlocks), 256, 0, st>>>(d_row_ptr.get(), rows, d_col.get(),
                                                                d_col_nnz.get(), maxcnt, wc, keys.get(),
-                                                               vals.get());
+                                                               perm_a.get());
     PSB_LAUNCH_CHECK();
-    const bool alt = radix_sort_pairs<uint64_t>(keys.get(), vals.get(), keys_alt.get(), vals_alt.get(),
+    const bool alt = radix_sort_pairs<uint64_t>(keys.get(), perm_a.get(), keys_alt.get(), perm_b.get(),
                                                 size_t(nnz), 0, wc + wr, st);
-    perm = alt ? std::move(vals_alt) : std::move(vals);
+    perm = alt ? perm_b.get() : perm_a.get();
   }
   d_col_nnz.release();
   trace.mark("freq_sort");
@@ -656,7 +827,7 @@ Matrix* build_matrix(int rows, int cols, int nnz, const int* row_ptr, const int*
     wa.sig[s] = sig[s].get();
   }
   group_signatures<<<grid_for(rows, 8, kBlocks), 256, 0, st>>>(d_row_ptr.get(), rows, S, fine, prefix.get(),
-                                                               perm.get(), d_col.get(), d_sigbit.get(), wa);
+                                                               perm, d_col.get(), d_sigbit.get(), wa);
   PSB_LAUNCH_CHECK();
   prefix.release();
   d_sigbit.release();
@@ -664,26 +835,37 @@ Matrix* build_matrix(int rows, int cols, int nnz, const int* row_ptr, const int*
 
   // --- Signature order of the groups of every workset: stable, lexicographically
   // descending over words (LSD: last word first, as utils/matrix_utils.cu:590-592).
+  // The worksets are independent, so each sorts on its own stream; within one, all
+  // word passes are queued without a host round trip (the buffer side of every
+  // pass is kept on the device), and the order ends in order[s].
   std::vector<DeviceArray<uint32_t>> order(S);
-  for (int s = 0; s < S; ++s) {
-    const int G = m->group_num[s];
-    order[s].reset(G);
-    if (!G) continue;
-    iota_u32(order[s].get(), G, st);
-    DeviceArray<uint32_t> keys(G), keys_alt(G), idx_alt(G);
-    uint32_t* idx = order[s].get();
-    uint32_t* idx2 = idx_alt.get();
-    for (int w = words - 1; w >= 0; --w) {
-      signature_word_keys<<<grid_for(G, 256, kBlocks), 256, 0, st>>>(sig[s].get() + size_t(w) * G, idx, G,
-                                                                     keys.get());
-      PSB_LAUNCH_CHECK();
-      if (radix_sort_pairs<uint32_t>(keys.get(), idx, keys_alt.get(), idx2, size_t(G), 0, 32, st))
-        std::swap(idx, idx2);
+  for (int s = 0; s < S; ++s) order[s].reset(m->group_num[s]);
+  {
+    StreamSet streams(S, st);
+    for (int s = 0; s < S; ++s) {
+      const int G = m->group_num[s];
+      if (G == 0) continue;
+      const cudaStream_t ss = streams[s];
+      const int per_word = radix_passes(size_t(G), 0, 32);
+      StreamArray<uint32_t> keys(2 * size_t(G), ss), idx_alt(G, ss);
+      StreamArray<int> side(size_t(words) * per_word + 1, ss);
+      PSB_CUDA(cudaMemsetAsync(side.get(), 0, sizeof(int), ss));
+      iota_u32(order[s].get(), G, ss);
+      int pass = 0;
+      for (int w = words - 1; w >= 0; --w) {
+        signature_word_keys<<<grid_for(G, 256, kBlocks), 256, 0, ss>>>(
+            sig[s].get() + size_t(w) * G, order[s].get(), idx_alt.get(), side.get() + pass, G, keys.get(),
+            keys.get() + G);
+        PSB_LAUNCH_CHECK();
+        radix_sort_pairs_async<uint32_t>(keys.get(), order[s].get(), keys.get() + G, idx_alt.get(), size_t(G), 0,
+                                         32, side.get() + pass, ss);
+        pass += per_word;
+      }
+      take_from_alt(side.get() + pass, idx_alt.get(), order[s].get(), size_t(G), ss);
     }
-    if (idx != order[s].get())
-      PSB_CUDA(cudaMemcpy(order[s].get(), idx, sizeof(uint32_t) * size_t(G), cudaMemcpyDeviceToDevice));
-    sig[s].release();
+    streams.join();
   }
+  for (int s = 0; s < S; ++s) sig[s].release();
   trace.mark("sig_sort");
 
   // --- Final worksets.
@@ -724,22 +906,24 @@ Matrix* build_matrix(int rows, int cols, int nnz, const int* row_ptr, const int*
       m->group_des[s] = des_out.release_ownership();
     }
     if (n == 0) continue;
-    DeviceArray<uint64_t> keys(n), keys_alt(n);
-    DeviceArray<uint32_t> vals(n), vals_alt(n);
+    const int wg = bits_for(unsigned(G - 1));
+    const int passes = radix_passes(size_t(n), 0, wcol + wg);
+    StreamArray<uint64_t> keys(n, st), keys_alt(n, st);
+    StreamArray<uint32_t> vals(n, st), vals_alt(n, st);
+    StreamArray<int> side(size_t(passes) + 1, st);
+    PSB_CUDA(cudaMemsetAsync(side.get(), 0, sizeof(int), st));
     gather_group_elements<<<grid_for(G, 8, kBlocks), 256, 0, st>>>(
         order[s].get(), G, s == 0 ? 0 : group_size(s), s == 0 ? res_off.get() : nullptr,
-        s == 0 ? res_size.get() : nullptr, src_start[s].get(), perm.get(), d_col.get(), wcol, keys.get(),
+        s == 0 ? res_size.get() : nullptr, src_start[s].get(), perm, d_col.get(), wcol, keys.get(),
         vals.get());
     PSB_LAUNCH_CHECK();
-    const int wg = bits_for(unsigned(G - 1));
-    const bool alt = radix_sort_pairs<uint64_t>(keys.get(), vals.get(), keys_alt.get(), vals_alt.get(),
-                                                size_t(n), 0, wcol + wg, st);
+    radix_sort_pairs_async<uint64_t>(keys.get(), vals.get(), keys_alt.get(), vals_alt.get(), size_t(n), 0,
+                                     wcol + wg, side.get(), st);
     DeviceArray<int> col_out(n), pos_out(n);
     DeviceArray<float> val_out(n);
-    finalize_workset<<<grid_for(n, 256, kBlocks), 256, 0, st>>>(alt ? keys_alt.get() : keys.get(),
-                                                                alt ? vals_alt.get() : vals.get(), n,
-                                                                (uint64_t(1) << wcol) - 1, d_val.get(),
-                                                                col_out.get(), val_out.get(), pos_out.get());
+    finalize_workset<<<grid_for(n, 256, kBlocks), 256, 0, st>>>(
+        keys.get(), vals.get(), keys_alt.get(), vals_alt.get(), side.get() + passes, n,
+        (uint64_t(1) << wcol) - 1, d_val.get(), col_out.get(), val_out.get(), pos_out.get());
     PSB_LAUNCH_CHECK();
     m->col_ind[s] = col_out.release_ownership();
     m->sp_data[s] = val_out.release_ownership();

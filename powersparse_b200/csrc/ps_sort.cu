@@ -8,6 +8,10 @@
 //   3. radix_scatter     : re-reads the tile, ranks every element among the
 //                          equal-digit elements before it (warp strips in order,
 //                          lanes in order: __match_any_sync peers), and writes it.
+// Which buffer pair holds the data is a device word per pass (`side`), read by the
+// kernels of the pass; the scatter writes the next pass's word.  So a sort queues
+// all its passes without a host round trip, and a pass whose digit is constant is
+// skipped on the device (every block sees the digit totals in the scanned counts).
 // Stability: tiles are ordered, warps own consecutive 512-element strips of a
 // tile, and within a 32-element chunk the rank counts lower lanes only.
 #include "ps_common.cuh"
@@ -99,11 +103,15 @@ constexpr int kRadixBits = 8;
 constexpr int kRadix = 1 << kRadixBits;
 constexpr int kSortWarps = kSortThreads / 32;
 constexpr int kStrip = kSortTile / kSortWarps;  // 512 consecutive elements per warp
+static_assert(kSortThreads == kRadix, "one thread per digit in the per-block digit loops");
 
 template <typename K>
-__global__ void __launch_bounds__(kSortThreads) radix_tile_hist(const K* __restrict__ keys, size_t n, int shift,
-                                                                uint32_t* __restrict__ counts,
+__global__ void __launch_bounds__(kSortThreads) radix_tile_hist(const K* __restrict__ keys0,
+                                                                const K* __restrict__ keys1,
+                                                                const int* __restrict__ side, size_t n,
+                                                                int shift, uint32_t* __restrict__ counts,
                                                                 size_t tiles) {
+  const K* __restrict__ keys = *side ? keys1 : keys0;
   __shared__ uint32_t hist[kRadix];
   hist[threadIdx.x] = 0;
   __syncthreads();
@@ -120,16 +128,30 @@ __global__ void __launch_bounds__(kSortThreads) radix_tile_hist(const K* __restr
   counts[size_t(threadIdx.x) * tiles + blockIdx.x] = hist[threadIdx.x];
 }
 
+// offsets: the scanned digit-major tile counts, kRadix * tiles + 1 entries (the last
+// is n), so digit d's first output position is offsets[d * tiles].  side[0]: where
+// the data is; side[1] (written by block 0): where this pass leaves it.
 template <typename K>
-__global__ void __launch_bounds__(kSortThreads) radix_scatter(const K* __restrict__ kin,
-                                                              const uint32_t* __restrict__ vin,
-                                                              K* __restrict__ kout,
-                                                              uint32_t* __restrict__ vout, size_t n,
+__global__ void __launch_bounds__(kSortThreads) radix_scatter(K* keys0, uint32_t* vals0, K* keys1,
+                                                              uint32_t* vals1, int* side, size_t n,
                                                               int shift,
                                                               const uint32_t* __restrict__ offsets,
                                                               size_t tiles) {
   __shared__ uint32_t whist[kSortWarps][kRadix];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int cur = side[0];
+  {
+    // kSortThreads == kRadix: thread d looks at digit d's total.
+    const int d = threadIdx.x;
+    const uint32_t total = offsets[size_t(d + 1) * tiles] - offsets[size_t(d) * tiles];
+    const bool constant = __syncthreads_or(size_t(total) == n) != 0;
+    if (blockIdx.x == 0 && threadIdx.x == 0) side[1] = constant ? cur : 1 - cur;
+    if (constant) return;  // every key has this digit: the pass is the identity
+  }
+  const K* __restrict__ kin = cur ? keys1 : keys0;
+  const uint32_t* __restrict__ vin = cur ? vals1 : vals0;
+  K* __restrict__ kout = cur ? keys0 : keys1;
+  uint32_t* __restrict__ vout = cur ? vals0 : vals1;
   for (int i = threadIdx.x; i < kSortWarps * kRadix; i += kSortThreads) (&whist[0][0])[i] = 0;
   __syncthreads();
   const size_t base = size_t(blockIdx.x) * kSortTile + size_t(warp) * kStrip;
@@ -182,9 +204,11 @@ __global__ void __launch_bounds__(kSortThreads) radix_scatter(const K* __restric
   }
 }
 
-__global__ void digit_starts(const uint32_t* __restrict__ offsets, size_t tiles, uint32_t* __restrict__ starts) {
-  const int d = threadIdx.x;
-  if (d <= kRadix) starts[d] = offsets[size_t(d) * tiles];
+__global__ void take_from_alt_kernel(const int* __restrict__ side, const uint32_t* __restrict__ alt,
+                                     uint32_t* __restrict__ primary, size_t n) {
+  if (!*side) return;
+  for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x)
+    primary[i] = alt[i];
 }
 
 __global__ void iota_kernel(uint32_t* v, size_t n) {
@@ -206,48 +230,58 @@ void exclusive_scan(const T* in, T* out, size_t n, cudaStream_t stream) {
     PSB_LAUNCH_CHECK();
     return;
   }
-  DeviceArray<T> partial(tiles + 1);
+  StreamArray<T> partial(tiles + 1, stream);
   scan_tile_reduce<T><<<unsigned(tiles), kScanThreads, 0, stream>>>(in, n, partial.get());
   PSB_LAUNCH_CHECK();
   exclusive_scan<T>(partial.get(), partial.get(), tiles, stream);
   scan_tile_apply<T><<<unsigned(tiles), kScanThreads, 0, stream>>>(in, out, n, partial.get());
   PSB_LAUNCH_CHECK();
-  PSB_CUDA(cudaStreamSynchronize(stream));  // partial is freed on return
+}
+
+int radix_passes(size_t n, int begin_bit, int end_bit) {
+  if (n <= 1 || end_bit <= begin_bit) return 0;
+  return (end_bit - begin_bit + kRadixBits - 1) / kRadixBits;
+}
+
+template <typename K>
+void radix_sort_pairs_async(K* keys, uint32_t* vals, K* keys_alt, uint32_t* vals_alt, size_t n,
+                            int begin_bit, int end_bit, int* side, cudaStream_t stream) {
+  const int passes = radix_passes(n, begin_bit, end_bit);
+  if (passes == 0) return;
+  if (n >= (size_t(1) << 32)) throw std::invalid_argument("radix sort: more than 2^32 - 1 elements");
+  const size_t tiles = (n + kSortTile - 1) / kSortTile;
+  StreamArray<uint32_t> offsets(size_t(kRadix) * tiles + 1, stream);
+  for (int p = 0; p < passes; ++p) {
+    const int shift = begin_bit + p * kRadixBits;
+    radix_tile_hist<K><<<unsigned(tiles), kSortThreads, 0, stream>>>(keys, keys_alt, side + p, n, shift,
+                                                                      offsets.get(), tiles);
+    PSB_LAUNCH_CHECK();
+    exclusive_scan<uint32_t>(offsets.get(), offsets.get(), size_t(kRadix) * tiles, stream);
+    radix_scatter<K><<<unsigned(tiles), kSortThreads, 0, stream>>>(keys, vals, keys_alt, vals_alt, side + p, n,
+                                                                    shift, offsets.get(), tiles);
+    PSB_LAUNCH_CHECK();
+  }
 }
 
 template <typename K>
 bool radix_sort_pairs(K* keys, uint32_t* vals, K* keys_alt, uint32_t* vals_alt, size_t n,
                       int begin_bit, int end_bit, cudaStream_t stream) {
-  if (n <= 1 || end_bit <= begin_bit) return false;
-  if (n >= (size_t(1) << 32)) throw std::invalid_argument("radix sort: more than 2^32 - 1 elements");
-  const size_t tiles = (n + kSortTile - 1) / kSortTile;
-  DeviceArray<uint32_t> offsets(size_t(kRadix) * tiles + 1);
-  DeviceArray<uint32_t> starts(kRadix + 1);
-  uint32_t h_starts[kRadix + 1];
-  bool in_alt = false;
-  for (int shift = begin_bit; shift < end_bit; shift += kRadixBits) {
-    const K* kin = in_alt ? keys_alt : keys;
-    const uint32_t* vin = in_alt ? vals_alt : vals;
-    K* kout = in_alt ? keys : keys_alt;
-    uint32_t* vout = in_alt ? vals : vals_alt;
-    radix_tile_hist<K><<<unsigned(tiles), kSortThreads, 0, stream>>>(kin, n, shift, offsets.get(), tiles);
-    PSB_LAUNCH_CHECK();
-    exclusive_scan<uint32_t>(offsets.get(), offsets.get(), size_t(kRadix) * tiles, stream);
-    digit_starts<<<1, kRadix + 1, 0, stream>>>(offsets.get(), tiles, starts.get());
-    PSB_LAUNCH_CHECK();
-    PSB_CUDA(cudaMemcpyAsync(h_starts, starts.get(), sizeof(h_starts), cudaMemcpyDeviceToHost, stream));
-    PSB_CUDA(cudaStreamSynchronize(stream));
-    bool constant = false;
-    for (int d = 0; d < kRadix; ++d)
-      if (size_t(h_starts[d + 1] - h_starts[d]) == n) constant = true;
-    if (constant) continue;  // every key has this digit: the pass is the identity
-    radix_scatter<K><<<unsigned(tiles), kSortThreads, 0, stream>>>(kin, vin, kout, vout, n, shift,
-                                                                    offsets.get(), tiles);
-    PSB_LAUNCH_CHECK();
-    in_alt = !in_alt;
-  }
+  const int passes = radix_passes(n, begin_bit, end_bit);
+  if (passes == 0) return false;
+  StreamArray<int> side(size_t(passes) + 1, stream);
+  PSB_CUDA(cudaMemsetAsync(side.get(), 0, sizeof(int), stream));
+  radix_sort_pairs_async<K>(keys, vals, keys_alt, vals_alt, n, begin_bit, end_bit, side.get(), stream);
+  int h_side = 0;
+  PSB_CUDA(cudaMemcpyAsync(&h_side, side.get() + passes, sizeof(int), cudaMemcpyDeviceToHost, stream));
   PSB_CUDA(cudaStreamSynchronize(stream));
-  return in_alt;
+  return h_side != 0;
+}
+
+void take_from_alt(const int* side, const uint32_t* alt, uint32_t* primary, size_t n, cudaStream_t stream) {
+  if (!n) return;
+  const unsigned blocks = unsigned(std::min<size_t>((n + 255) / 256, size_t(8) * device_sms()));
+  take_from_alt_kernel<<<blocks, 256, 0, stream>>>(side, alt, primary, n);
+  PSB_LAUNCH_CHECK();
 }
 
 void iota_u32(uint32_t* vals, size_t n, cudaStream_t stream) {
@@ -260,6 +294,10 @@ void iota_u32(uint32_t* vals, size_t n, cudaStream_t stream) {
 template void exclusive_scan<int32_t>(const int32_t*, int32_t*, size_t, cudaStream_t);
 template void exclusive_scan<uint32_t>(const uint32_t*, uint32_t*, size_t, cudaStream_t);
 template void exclusive_scan<int64_t>(const int64_t*, int64_t*, size_t, cudaStream_t);
+template void radix_sort_pairs_async<uint32_t>(uint32_t*, uint32_t*, uint32_t*, uint32_t*, size_t, int, int,
+                                               int*, cudaStream_t);
+template void radix_sort_pairs_async<uint64_t>(uint64_t*, uint32_t*, uint64_t*, uint32_t*, size_t, int, int,
+                                               int*, cudaStream_t);
 template bool radix_sort_pairs<uint32_t>(uint32_t*, uint32_t*, uint32_t*, uint32_t*, size_t, int, int,
                                          cudaStream_t);
 template bool radix_sort_pairs<uint64_t>(uint64_t*, uint32_t*, uint64_t*, uint32_t*, size_t, int, int,
