@@ -130,3 +130,28 @@ def test_csr_positions_match_the_oracle(name):
         got = m.download()
     for s in range(L.S):
         assert np.array_equal(got[f"ws{s}_pos"], L.csr_pos[s]), (name, s)
+
+
+def test_preprocess_trace_reports_every_phase_and_changes_nothing(capfd, monkeypatch):
+    """PSB_PREPROCESS_TRACE=1 prints one line of per-phase wall times to stderr; the
+    layout built with it is the layout built without it."""
+    A = synth.config_matrix(2, scale=0.01)
+    monkeypatch.delenv("PSB_PREPROCESS_TRACE", raising=False)
+    with psb.PowerSparseMatrixGPU(A.rows, A.cols, A.nnz, A.row_ptr, A.col_ind, A.values) as m:
+        plain = m.download()
+    assert "psb preprocess:" not in capfd.readouterr().err
+    monkeypatch.setenv("PSB_PREPROCESS_TRACE", "1")
+    with psb.PowerSparseMatrixGPU(A.rows, A.cols, A.nnz, A.row_ptr, A.col_ind, A.values) as m:
+        traced = m.download()
+    lines = [l for l in capfd.readouterr().err.splitlines() if l.startswith("psb preprocess:")]
+    assert len(lines) == 1, lines
+    phases = dict(kv.split("=") for kv in lines[0].split(":", 1)[1].split())
+    assert list(phases) == ["validate", "upload", "worksets", "col_freq", "freq_sort", "groups", "sig_bits_wait",
+                            "signatures", "sig_sort", "residue_meta", "col_sort", "tasks"]
+    assert all(float(v) >= 0.0 for v in phases.values())
+    assert plain.keys() == traced.keys()
+    for k in plain:
+        if isinstance(plain[k], np.ndarray):
+            assert np.array_equal(plain[k], traced[k]), k
+        else:
+            assert plain[k] == traced[k], k
