@@ -181,6 +181,35 @@ int ps_spmm_values(const ps_matrix* matrix, int N, const float* values, const fl
  * row structure is the matrix's own.  No reference counterpart. */
 int ps_edge_softmax_csr(const ps_matrix* matrix, float* values, void* stream);
 
+/* SpMM fused with the all-gather of its result across GPUs.  No reference
+ * counterpart (the reference is single-GPU).  For row panels on several GPUs whose
+ * results every GPU needs whole (the next layer's dense operand): instead of SpMM
+ * and then an all-gather, each finished row of C is stored straight into the other
+ * GPUs' copies while the kernel still runs.  C (+)= A * B exactly as ps_spmm (same
+ * B, C, stream rules), and every row of C, once its last contribution of this call
+ * has been added, is also stored to peers[k] + row * N for k < n_peers.  peers is a
+ * host array of n_peers (0..7) device pointers that this GPU can write (another
+ * GPU's buffer opened with ps_ipc_open, or a buffer of this GPU), each pointing at
+ * the row of that replica that corresponds to this matrix's row 0.  N is 32, 64 or
+ * 128.  The first call at N < 128 and the first at N = 128 each count, once, how
+ * many contributions every row receives (allocates, synchronous, cannot be
+ * captured).  Eager calls on one matrix are ordered on the device by the library.
+ * A peer's replica is complete once every GPU's call has completed (for example
+ * after a collective that follows the call on every GPU); the caller must not let a
+ * peer read or overwrite those rows while calls that write them may run. */
+int ps_spmm_push(const ps_matrix* matrix, int N, const float* B, float* C, float* const* peers, int n_peers,
+                 void* stream);
+
+/* CUDA IPC for ps_spmm_push's peer replicas.  ps_ipc_export writes the IPC handle
+ * (PS_IPC_HANDLE_BYTES bytes) of the device allocation that holds `ptr` and ptr's
+ * byte offset in it; another process opens the handle with ps_ipc_open (the
+ * allocation's base address in that process, peer access enabled on demand) and
+ * releases it with ps_ipc_close.  No reference counterpart. */
+#define PS_IPC_HANDLE_BYTES 64
+int ps_ipc_export(const void* ptr, unsigned char* handle, unsigned long long* offset);
+int ps_ipc_open(const unsigned char* handle, void** base);
+int ps_ipc_close(void* base);
+
 /* nnz-balanced contiguous row panels for `parts` GPUs: writes cuts[0..parts]
  * with cuts[0] = 0, cuts[parts] = row_num, nondecreasing, panel p = rows
  * [cuts[p], cuts[p+1]).  Cut p is the first row whose row_ptr reaches

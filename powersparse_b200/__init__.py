@@ -84,7 +84,13 @@ _SIGNATURES = [
     ("ps_spmm_values", ctypes.c_int, [_vp, ctypes.c_int, _vp, _vp, _vp, _vp]),
     ("ps_edge_softmax_csr", ctypes.c_int, [_vp, _vp, _vp]),
     ("ps_partition_rows", ctypes.c_int, [ctypes.c_int, _i32p, ctypes.c_int, _i32p]),
+    ("ps_spmm_push", ctypes.c_int, [_vp, ctypes.c_int, _vp, _vp, ctypes.POINTER(_vp), ctypes.c_int, _vp]),
+    ("ps_ipc_export", ctypes.c_int, [_vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_ulonglong)]),
+    ("ps_ipc_open", ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(_vp)]),
+    ("ps_ipc_close", ctypes.c_int, [_vp]),
 ]
+
+PS_IPC_HANDLE_BYTES = 64
 
 
 def GROUP_SIZE(s: int) -> int:
@@ -332,6 +338,36 @@ def SpMM_values(matrix: PowerSparseMatrixGPU, N: int, values, B, C, stream=None)
 def edge_softmax_csr(matrix: PowerSparseMatrixGPU, values, stream=None) -> None:
     """In place: softmax over each row's edge values (nnz floats, CSR order)."""
     _check(load_library().ps_edge_softmax_csr(matrix.handle, _dev_ptr(values), _stream_ptr(stream)))
+
+
+def SpMM_push(matrix: PowerSparseMatrixGPU, N: int, B, C, peers: Sequence[int], stream=None) -> None:
+    """C (+)= A·B as SpMM, with every finished row of C also stored to each peer replica
+    (``peers``: device addresses of the replicas' rows matching this matrix's row 0)."""
+    arr = (_vp * max(1, len(peers)))(*[_vp(int(p)) for p in peers])
+    _check(load_library().ps_spmm_push(matrix.handle, int(N), _dev_ptr(B), _dev_ptr(C), arr, len(peers),
+                                       _stream_ptr(stream)))
+
+
+def ipc_export(tensor) -> tuple:
+    """(CUDA IPC handle bytes, byte offset) of the device allocation holding ``tensor``."""
+    handle = ctypes.create_string_buffer(PS_IPC_HANDLE_BYTES)
+    offset = ctypes.c_ulonglong(0)
+    _check(load_library().ps_ipc_export(_dev_ptr(tensor), handle, ctypes.byref(offset)))
+    return handle.raw, int(offset.value)
+
+
+def ipc_open(handle: bytes) -> int:
+    """Opens a handle from ipc_export in another process; returns the allocation's base address."""
+    if len(handle) != PS_IPC_HANDLE_BYTES:
+        raise ValueError("an IPC handle is %d bytes" % PS_IPC_HANDLE_BYTES)
+    base = _vp()
+    _check(load_library().ps_ipc_open(handle, ctypes.byref(base)))
+    return int(base.value)
+
+
+def ipc_close(base: int) -> None:
+    """Releases a mapping made by ipc_open."""
+    _check(load_library().ps_ipc_close(_vp(int(base))))
 
 
 def partition_rows(row_ptr, parts: int) -> np.ndarray:

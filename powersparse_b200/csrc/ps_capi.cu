@@ -1,11 +1,14 @@
 // extern "C" boundary of libpowersparse_b200.so (declared in include/powersparse_b200.h).
 #include "powersparse_b200.h"
 
+#include <cuda.h>
+
 #include "ps_common.cuh"
 #include "ps_matrix.h"
 #include "ps_ops.h"
 
 #include <algorithm>
+#include <cstring>
 #include <exception>
 #include <new>
 #include <stdexcept>
@@ -40,6 +43,22 @@ int guarded(F&& f) {
 }
 
 const psb::Matrix& M(const ps_matrix* h) { return *reinterpret_cast<const psb::Matrix*>(h); }
+
+// cuMemGetAddressRange from the driver, looked up at run time (the library links the
+// runtime only): the allocation that holds a device pointer, whose base is what a
+// CUDA IPC handle names.
+using AddressRangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+AddressRangeFn address_range() {
+  static AddressRangeFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    PSB_CUDA(cudaGetDriverEntryPointByVersion("cuMemGetAddressRange", &p, 12000, cudaEnableDefault, &q));
+    if (q != cudaDriverEntryPointSuccess || !p)
+      throw psb::CudaError(cudaErrorNotSupported, "cuMemGetAddressRange is not available from the driver");
+    return reinterpret_cast<AddressRangeFn>(p);
+  }();
+  return fn;
+}
 
 void require_device(const psb::Matrix& m) {
   int dev = -1;
@@ -158,6 +177,50 @@ int ps_sddmm(const ps_matrix* h, int N, const float* lhs, const float* rhs, floa
     }
     require_device(m);
     psb::sddmm_launch(m, N, lhs, rhs, out, static_cast<cudaStream_t>(stream));
+  });
+}
+
+int ps_spmm_push(const ps_matrix* h, int N, const float* B, float* C, float* const* peers, int n_peers,
+                 void* stream) {
+  return guarded([&] {
+    if (!h || !B || !C) throw std::invalid_argument("Invalid SpMM buffers or stream count");
+    const psb::Matrix& m = M(h);
+    require_device(m);
+    psb::spmm_push_launch(m, N, B, C, peers, n_peers, static_cast<cudaStream_t>(stream));
+  });
+}
+
+int ps_ipc_export(const void* ptr, unsigned char* handle, unsigned long long* offset) {
+  return guarded([&] {
+    if (!ptr || !handle || !offset) throw std::invalid_argument("ps_ipc_export: null argument");
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    const CUresult r = address_range()(&base, &size, reinterpret_cast<CUdeviceptr>(ptr));
+    if (r != CUDA_SUCCESS)
+      throw std::invalid_argument("ps_ipc_export: not a device allocation (cuMemGetAddressRange error " +
+                                  std::to_string(int(r)) + ")");
+    cudaIpcMemHandle_t h;
+    PSB_CUDA(cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)));
+    static_assert(sizeof(h) == PS_IPC_HANDLE_BYTES, "CUDA IPC handle size");
+    std::memcpy(handle, &h, sizeof(h));
+    *offset = static_cast<unsigned long long>(reinterpret_cast<CUdeviceptr>(ptr) - base);
+  });
+}
+
+int ps_ipc_open(const unsigned char* handle, void** base) {
+  return guarded([&] {
+    if (!handle || !base) throw std::invalid_argument("ps_ipc_open: null argument");
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    *base = nullptr;
+    PSB_CUDA(cudaIpcOpenMemHandle(base, h, cudaIpcMemLazyEnablePeerAccess));
+  });
+}
+
+int ps_ipc_close(void* base) {
+  return guarded([&] {
+    if (!base) throw std::invalid_argument("ps_ipc_close: null pointer");
+    PSB_CUDA(cudaIpcCloseMemHandle(base));
   });
 }
 

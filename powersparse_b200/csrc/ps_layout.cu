@@ -54,6 +54,10 @@ Matrix::~Matrix() {
   cudaFree(wide_acc);
   for (auto p : wide_acc_retired) cudaFree(p);
   if (wide_ready) cudaEventDestroy(wide_ready);
+  for (auto p : push_count) cudaFree(p);
+  cudaFree(push_pending);
+  cudaFree(quiet_rows);
+  if (push_ready) cudaEventDestroy(push_ready);
 }
 
 namespace {

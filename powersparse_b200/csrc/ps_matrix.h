@@ -91,6 +91,17 @@ struct Matrix {
   mutable cudaEvent_t wide_ready = nullptr;
   mutable std::mutex wide_mutex;
 
+  // SpMM with a push epilogue (ps_spmm_push), built by its first call per residue
+  // cut: push_count[cut][r] = how many times one launch adds into row r of C (0 for
+  // wide rows, which the fold kernel finishes); push_pending is the per-call
+  // countdown; quiet_rows lists the rows nothing adds into (not wide, no elements).
+  mutable int* push_count[2] = {nullptr, nullptr};
+  mutable int* push_pending = nullptr;
+  mutable int* quiet_rows = nullptr;
+  mutable int num_quiet_rows = -1;     // -1: not built yet
+  mutable cudaEvent_t push_ready = nullptr;  // orders eager push calls (they share push_pending)
+  mutable std::mutex push_mutex;
+
   Matrix() = default;
   Matrix(const Matrix&) = delete;
   Matrix& operator=(const Matrix&) = delete;
@@ -140,5 +151,8 @@ constexpr int kWideRowSlices = 8;
 // time; plain FP32 chunk sums 0.99 / 1.32; exact products 0.14 on rows of >= 65536.
 enum WideSum { kWideQuad = 0, kWideExact = 1 };
 constexpr int kExactRowSlices = 256;
+
+// Peer replicas one ps_spmm_push call writes (a node of 8 GPUs: 7 peers).
+constexpr int kMaxPushPeers = 7;
 
 }  // namespace psb

@@ -137,7 +137,30 @@ struct SpmmArgs {
   const int* pos_ws[kMaxWorksets];  // CSR position of every element (kValues)
   const float* values;              // per-call values in CSR order (kValues)
   int S, rows, cols, nnz, wide_rows;  // index limits (checked build)
+  // kPush: per-row countdown of the adds into C still to come in this launch, and
+  // the peer replicas (other GPUs' copies of C, at this panel's first row).
+  int* pending;
+  float* peer[kMaxPushPeers];
+  int peers;
 };
+
+// kPush epilogue of one add into row `row` of C: counts the add down and, in the
+// lane group that made the row's last add, stores the finished row segment to every
+// peer replica.  Each lane fences its own atomic add before lane 0 counts, so the
+// finishing group reads complete sums from L2; no lane ever waits for another group.
+template <int LG>
+__device__ __forceinline__ void push_if_finished(const SpmmArgs& a, long long row, int colofs, unsigned gm,
+                                                 int l) {
+  __threadfence();
+  __syncwarp(gm);
+  int last = 0;
+  if (l == 0) last = atomicSub(a.pending + row, 1) == 1;
+  last = __shfl_sync(gm, last, 0, LG);
+  if (!last) return;
+  __threadfence();
+  const float4 v = __ldcg(reinterpret_cast<const float4*>(a.C + row * a.ldb + colofs));
+  for (int k = 0; k < a.peers; ++k) __stcg(reinterpret_cast<float4*>(a.peer[k] + row * a.ldb + colofs), v);
+}
 
 // Checked build: a task must lie inside its workset (begin <= end <= workset length,
 // group < groups) and name an existing wide-row slot.
@@ -162,8 +185,9 @@ __device__ __forceinline__ bool task_ok(const Args& a, const Task& t) {
 // per 32-element chunk and carry the running sum in FP64; slices of wide rows add
 // that FP64 sum into the row's FP64 scratch instead of into C (Matrix::wide_rows).
 // With kValues the value of element e is a.values[csr_pos[e]] (values supplied per
-// call in CSR order) instead of the layout's sp_data[e].
-template <int LG, bool kValues = false>
+// call in CSR order) instead of the layout's sp_data[e].  With kPush every add into
+// C is followed by push_if_finished.
+template <int LG, bool kValues = false, bool kPush = false>
 __global__ void __launch_bounds__(kThreads, 4) spmm_fused(const SpmmArgs a) {
   constexpr int NG = 32 / LG;
   // Column indices and values of the staged chunk, read back 4 at a time (one
@@ -255,7 +279,10 @@ __global__ void __launch_bounds__(kThreads, 4) spmm_fused(const SpmmArgs a) {
             const int w = sr[j + u];
             if (w != sr[j + u + 1]) {
               const int row = w & 0x7fffffff;
-              if (in_range(row, a.rows, kBadRow)) emit4(Cl + (long long)row * a.ldb, acc, w < 0);
+              if (in_range(row, a.rows, kBadRow)) {
+                emit4(Cl + (long long)row * a.ldb, acc, w < 0);
+                if constexpr (kPush) push_if_finished<LG>(a, row, colofs, gm, l);
+              }
               acc = make_float4(0.f, 0.f, 0.f, 0.f);
             }
           }
@@ -373,8 +400,10 @@ __global__ void __launch_bounds__(kThreads, 4) spmm_fused(const SpmmArgs a) {
         atomicAdd(row_sum + 2, dz);
         atomicAdd(row_sum + 3, dw);
       } else {
-        if (in_range(g, a.ws.groups[t.ws], kBadGroup) && in_range(des[g], a.rows, kBadRow))
+        if (in_range(g, a.ws.groups[t.ws], kBadGroup) && in_range(des[g], a.rows, kBadRow)) {
           emit4(Cl + (long long)des[g] * a.ldb, make_float4(float(dx), float(dy), float(dz), float(dw)), true);
+          if constexpr (kPush) push_if_finished<LG>(a, des[g], colofs, gm, l);
+        }
       }
       dx = dy = dz = dw = 0.0;
       ++g;
@@ -588,8 +617,16 @@ __global__ void __launch_bounds__(kThreads, LG == 8 ? 4 : 3) sddmm_fused(const S
 
 // C[wide_row[slot], :] = float(C + acc[slot, :]) (one rounding), then acc = 0
 // so that the scratch is all-zero for the next call.
+// The peer replicas of a push call (n = 0 outside ps_spmm_push).
+struct PeerSet {
+  float* p[kMaxPushPeers];
+  int n;
+};
+
+// With peers, the finished row is also stored to every peer replica.
 __global__ void __launch_bounds__(256) wide_rows_fold(const int* __restrict__ wide_row, int wide_rows, int N,
-                                                      double* __restrict__ acc, float* __restrict__ C, int rows) {
+                                                      double* __restrict__ acc, float* __restrict__ C, int rows,
+                                                      const PeerSet peers) {
   const int per_row = N / 4;
   const long long total = (long long)wide_rows * per_row;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
@@ -597,7 +634,8 @@ __global__ void __launch_bounds__(256) wide_rows_fold(const int* __restrict__ wi
     const long long slot = i / per_row;
     const int q = int(i - slot * per_row);
     double2* a2 = reinterpret_cast<double2*>(acc + slot * N + 4 * q);
-    float4* c4 = reinterpret_cast<float4*>(C + checked(wide_row[slot], rows, kBadRow) * N + 4 * q);
+    const long long off = checked(wide_row[slot], rows, kBadRow) * N + 4 * q;
+    float4* c4 = reinterpret_cast<float4*>(C + off);
     const double2 lo = a2[0], hi = a2[1];
     float4 c = *c4;
     c.x = float(double(c.x) + lo.x);
@@ -605,9 +643,58 @@ __global__ void __launch_bounds__(256) wide_rows_fold(const int* __restrict__ wi
     c.z = float(double(c.z) + hi.x);
     c.w = float(double(c.w) + hi.y);
     *c4 = c;
+    for (int k = 0; k < peers.n; ++k) __stcg(reinterpret_cast<float4*>(peers.p[k] + off), c);
     a2[0] = make_double2(0.0, 0.0);
     a2[1] = make_double2(0.0, 0.0);
   }
+}
+
+// Stores rows `list[i]` of C (N floats each) to every peer replica.
+__global__ void __launch_bounds__(256) push_rows(const int* __restrict__ list, int count, int N,
+                                                 const float* __restrict__ C, int rows, const PeerSet peers) {
+  const int per_row = N / 4;
+  const long long total = (long long)count * per_row;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long k = i / per_row;
+    const long long off = checked(list[k], rows, kBadRow) * N + 4 * (i - k * per_row);
+    const float4 v = *reinterpret_cast<const float4*>(C + off);
+    for (int p = 0; p < peers.n; ++p) __stcg(reinterpret_cast<float4*>(peers.p[p] + off), v);
+  }
+}
+
+// Adds into C per row of one SpMM launch over the task lists of `a`, counted the way
+// spmm_fused adds: a block task that is not a wide-row slice adds once per group it
+// ends; a residue task once per run of equal row words (and at its end).
+__global__ void __launch_bounds__(256) count_row_adds(const SpmmArgs a, int* __restrict__ count) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < a.num_tasks; i += gridDim.x * blockDim.x) {
+    const Task t = i < a.num_block ? a.block_tasks[i] : a.res_tasks[i - a.num_block];
+    if (!task_ok(a, t)) continue;
+    if (t.ws == 0) {
+      if (t.end <= t.begin) continue;
+      int prev = a.res_row[t.begin];
+      for (int e = t.begin + 1; e < t.end; ++e) {
+        const int w = a.res_row[e];
+        if (w != prev) {
+          if (in_range(prev & 0x7fffffff, a.rows, kBadRow)) atomicAdd(count + (prev & 0x7fffffff), 1);
+          prev = w;
+        }
+      }
+      if (in_range(prev & 0x7fffffff, a.rows, kBadRow)) atomicAdd(count + (prev & 0x7fffffff), 1);
+    } else if (t.slot < 0) {
+      const int G = a.ws.group_len[t.ws];
+      const int* des = a.ws.des[t.ws];
+      for (int g = t.begin / G; (long long)g * G < t.end; ++g)
+        if (in_range(g, a.ws.groups[t.ws], kBadGroup) && in_range(des[g], a.rows, kBadRow))
+          atomicAdd(count + des[g], 1);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256) zero_listed(const int* __restrict__ list, int count, int* __restrict__ v,
+                                                   int rows) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < count; i += gridDim.x * blockDim.x)
+    v[checked(list[i], rows, kBadRow)] = 0;
 }
 
 // In-place softmax over each row's entries of a CSR-order array (one warp per row):
@@ -712,8 +799,16 @@ void check_bounds(cudaStream_t stream) {
   }
 }
 
-template <bool kValues>
-void spmm_run(const Matrix& m, int N, const float* B, float* C, const float* values, cudaStream_t stream) {
+// The pieces of a push call beyond plain SpMM (kPush): the per-row countdown and
+// the peer replicas.
+struct PushSetup {
+  int* pending = nullptr;
+  PeerSet peers{};
+};
+
+template <bool kValues, bool kPush = false>
+void spmm_run(const Matrix& m, int N, const float* B, float* C, const float* values, cudaStream_t stream,
+              const PushSetup& push = PushSetup{}) {
   SpmmArgs a{};
   if (!set_tasks(a, m, N)) return;
   a.ws = view_of(m);
@@ -725,13 +820,18 @@ void spmm_run(const Matrix& m, int N, const float* B, float* C, const float* val
     for (int s = 0; s < m.S; ++s) a.pos_ws[s] = m.csr_pos[s];
     a.values = values;
   }
+  if constexpr (kPush) {
+    a.pending = push.pending;
+    for (int k = 0; k < push.peers.n; ++k) a.peer[k] = push.peers.p[k];
+    a.peers = push.peers.n;
+  }
   auto launch = [&] {
     if (N % 128 == 0) {
-      spmm_fused<32, kValues><<<dim3(task_blocks(a.num_tasks, 32), N / 128), kThreads, 0, stream>>>(a);
+      spmm_fused<32, kValues, kPush><<<dim3(task_blocks(a.num_tasks, 32), N / 128), kThreads, 0, stream>>>(a);
     } else if (N % 64 == 0) {
-      spmm_fused<16, kValues><<<dim3(task_blocks(a.num_tasks, 16), N / 64), kThreads, 0, stream>>>(a);
+      spmm_fused<16, kValues, kPush><<<dim3(task_blocks(a.num_tasks, 16), N / 64), kThreads, 0, stream>>>(a);
     } else {
-      spmm_fused<8, kValues><<<dim3(task_blocks(a.num_tasks, 8), N / 32), kThreads, 0, stream>>>(a);
+      spmm_fused<8, kValues, kPush><<<dim3(task_blocks(a.num_tasks, 8), N / 32), kThreads, 0, stream>>>(a);
     }
     PSB_LAUNCH_CHECK();
   };
@@ -765,10 +865,59 @@ void spmm_run(const Matrix& m, int N, const float* B, float* C, const float* val
   launch();
   const long long total = (long long)m.wide_rows * (N / 4);
   const unsigned blocks = unsigned(std::min<long long>((total + 255) / 256, 8LL * device_sms()));
-  wide_rows_fold<<<blocks, 256, 0, stream>>>(m.wide_row, m.wide_rows, N, m.wide_acc, C, m.rows);
+  wide_rows_fold<<<blocks, 256, 0, stream>>>(m.wide_row, m.wide_rows, N, m.wide_acc, C, m.rows,
+                                             kPush ? push.peers : PeerSet{});
   PSB_LAUNCH_CHECK();
   if (capture == cudaStreamCaptureStatusNone) PSB_CUDA(cudaEventRecord(m.wide_ready, stream));
   check_bounds(stream);
+}
+
+// First push call at a residue cut: the per-row add counts (wide rows zeroed: the
+// fold finishes them), the countdown buffer, the list of rows nothing adds into and
+// the event that orders eager push calls.  Synchronous; caller holds push_mutex.
+void prepare_push(const Matrix& m, int N, cudaStream_t stream) {
+  const int cut = N < 128 ? kFineResidue : kCoarseResidue;
+  if (m.push_count[cut]) return;
+  SpmmArgs a{};
+  set_tasks(a, m, N);
+  a.ws = view_of(m);
+  a.res_row = m.residue_row;
+  DeviceArray<int> count(size_t(m.rows));
+  PSB_CUDA(cudaMemsetAsync(count.get(), 0, sizeof(int) * size_t(m.rows), stream));
+  const unsigned blocks = unsigned(std::max(1LL, std::min<long long>((a.num_tasks + 255) / 256, 8LL * device_sms())));
+  count_row_adds<<<blocks, 256, 0, stream>>>(a, count.get());
+  PSB_LAUNCH_CHECK();
+  if (m.wide_rows > 0) {
+    zero_listed<<<unsigned(std::min<long long>((m.wide_rows + 255) / 256, 8LL * device_sms())), 256, 0, stream>>>(
+        m.wide_row, m.wide_rows, count.get(), m.rows);
+    PSB_LAUNCH_CHECK();
+  }
+  PSB_CUDA(cudaStreamSynchronize(stream));
+  check_bounds(stream);
+  if (m.num_quiet_rows < 0) {
+    // Rows that no add reaches and that are not wide: no elements at all (the same
+    // rows at either residue cut).
+    std::vector<int> h_count(size_t(m.rows)), h_wide(size_t(m.wide_rows)), quiet;
+    PSB_CUDA(cudaMemcpy(h_count.data(), count.get(), sizeof(int) * h_count.size(), cudaMemcpyDeviceToHost));
+    if (m.wide_rows > 0)
+      PSB_CUDA(cudaMemcpy(h_wide.data(), m.wide_row, sizeof(int) * h_wide.size(), cudaMemcpyDeviceToHost));
+    std::vector<char> wide(size_t(m.rows), 0);
+    for (int r : h_wide) wide[size_t(r)] = 1;
+    for (int r = 0; r < m.rows; ++r)
+      if (h_count[size_t(r)] == 0 && !wide[size_t(r)]) quiet.push_back(r);
+    if (!quiet.empty()) {
+      DeviceArray<int> d_quiet(quiet.size());
+      PSB_CUDA(cudaMemcpy(d_quiet.get(), quiet.data(), sizeof(int) * quiet.size(), cudaMemcpyHostToDevice));
+      m.quiet_rows = d_quiet.release_ownership();
+    }
+    m.num_quiet_rows = int(quiet.size());
+  }
+  if (!m.push_pending) {
+    DeviceArray<int> pending(size_t(m.rows));
+    m.push_pending = pending.release_ownership();
+  }
+  if (!m.push_ready) PSB_CUDA(cudaEventCreateWithFlags(&m.push_ready, cudaEventDisableTiming));
+  m.push_count[cut] = count.release_ownership();
 }
 
 }  // namespace
@@ -780,6 +929,43 @@ void spmm_launch(const Matrix& m, int N, const float* B, float* C, cudaStream_t 
 void spmm_values_launch(const Matrix& m, int N, const float* values, const float* B, float* C,
                         cudaStream_t stream) {
   spmm_run<true>(m, N, B, C, values, stream);
+}
+
+void spmm_push_launch(const Matrix& m, int N, const float* B, float* C, float* const* peers, int n_peers,
+                      cudaStream_t stream) {
+  if (N != 32 && N != 64 && N != 128)
+    throw std::invalid_argument("ps_spmm_push: N must be 32, 64 or 128 (one column slab per row)");
+  if (n_peers < 0 || n_peers > kMaxPushPeers)
+    throw std::invalid_argument("ps_spmm_push: between 0 and " + std::to_string(kMaxPushPeers) + " peers");
+  if (n_peers > 0 && !peers) throw std::invalid_argument("ps_spmm_push: null peer array");
+  PushSetup push;
+  for (int k = 0; k < n_peers; ++k) {
+    if (!peers[k]) throw std::invalid_argument("ps_spmm_push: null peer replica");
+    push.peers.p[k] = peers[k];
+  }
+  push.peers.n = n_peers;
+  std::lock_guard<std::mutex> lock(m.push_mutex);
+  cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+  PSB_CUDA(cudaStreamIsCapturing(stream, &capture));
+  const int cut = N < 128 ? kFineResidue : kCoarseResidue;
+  if (!m.push_count[cut]) {
+    if (capture != cudaStreamCaptureStatusNone)
+      throw std::runtime_error("ps_spmm_push at a new N cannot be captured: call it once with this N first");
+    prepare_push(m, N, stream);
+  }
+  if (capture == cudaStreamCaptureStatusNone) PSB_CUDA(cudaStreamWaitEvent(stream, m.push_ready, 0));
+  PSB_CUDA(cudaMemcpyAsync(m.push_pending, m.push_count[cut], sizeof(int) * size_t(m.rows),
+                           cudaMemcpyDeviceToDevice, stream));
+  push.pending = m.push_pending;
+  spmm_run<false, true>(m, N, B, C, nullptr, stream, push);
+  if (m.num_quiet_rows > 0 && n_peers > 0) {
+    const long long total = (long long)m.num_quiet_rows * (N / 4);
+    const unsigned blocks = unsigned(std::min<long long>((total + 255) / 256, 8LL * device_sms()));
+    push_rows<<<blocks, 256, 0, stream>>>(m.quiet_rows, m.num_quiet_rows, N, C, m.rows, push.peers);
+    PSB_LAUNCH_CHECK();
+  }
+  if (capture == cudaStreamCaptureStatusNone) PSB_CUDA(cudaEventRecord(m.push_ready, stream));
+  check_bounds(stream);
 }
 
 void edge_softmax_launch(const Matrix& m, float* values, cudaStream_t stream) {
@@ -899,7 +1085,7 @@ void spmm_launch_noalloc(const Matrix& m, int N, const float* B, float* C, cudaS
   if (m.wide_rows > 0) {
     const long long total = (long long)m.wide_rows * (N / 4);
     const unsigned blocks = unsigned(std::min<long long>((total + 255) / 256, 8LL * device_sms()));
-    wide_rows_fold<<<blocks, 256, 0, stream>>>(m.wide_row, m.wide_rows, N, a.wide_acc, C, m.rows);
+    wide_rows_fold<<<blocks, 256, 0, stream>>>(m.wide_row, m.wide_rows, N, a.wide_acc, C, m.rows, PeerSet{});
     PSB_LAUNCH_CHECK();
   }
   check_bounds(stream);

@@ -15,6 +15,14 @@ void spmm_launch(const Matrix& m, int N, const float* B, float* C, cudaStream_t 
 void spmm_values_launch(const Matrix& m, int N, const float* values, const float* B, float* C,
                         cudaStream_t stream);
 
+// spmm_launch whose finished rows are also stored to `n_peers` peer replicas (device
+// pointers, possibly on other GPUs, each at this panel's first row): a row is stored
+// by the lane group that makes its last add into C, by the wide-row fold, or (rows
+// without elements) by a copy kernel.  N is 32, 64 or 128.  The first call at a
+// residue cut builds the per-row add counts (allocates, synchronous).
+void spmm_push_launch(const Matrix& m, int N, const float* B, float* C, float* const* peers, int n_peers,
+                      cudaStream_t stream);
+
 // In place, for every row r: values[p] = softmax over p in [row_ptr[r], row_ptr[r+1])
 // (values: device, CSR order, MatrixNNZ() floats).
 void edge_softmax_launch(const Matrix& m, float* values, cudaStream_t stream);

@@ -17,10 +17,10 @@ from typing import Optional
 
 import numpy as np
 
-from . import PowerSparseMatrixGPU, SDDMM, SpMM, partition_rows
+from . import PowerSparseMatrixGPU, SDDMM, SpMM, SpMM_push, ipc_close, ipc_export, ipc_open, partition_rows
 from .synth import Csr
 
-__all__ = ["panel_csr", "ShardedPowerSparse", "allgather_rows", "heartbeat", "PeerLost"]
+__all__ = ["panel_csr", "ShardedPowerSparse", "allgather_rows", "heartbeat", "PeerLost", "Replicas"]
 
 
 class PeerLost(RuntimeError):
@@ -130,6 +130,26 @@ class ShardedPowerSparse:
             return allgather_rows(C_local, self.cuts, group)
         return C_local
 
+    def spmm_replicated(self, N: int, B, replicas: "Replicas", stream=None, group=None):
+        """The full C = A · B on every rank in ``replicas.full``: this rank's SpMM writes
+        its panel of its own replica and stores every finished row straight into the
+        other ranks' replicas over NVLink (ps_spmm_push: the all-gather fused into the
+        SpMM, no separate collective moves C).  The panel is accumulated into, as SpMM
+        does: zero it first for a fresh product.  Returns after a one-element all-reduce
+        queued behind the SpMM, so on return (in stream order) every rank's pushes into
+        this rank's replica have completed."""
+        import torch
+        import torch.distributed as dist
+        r0, r1 = self.row_begin, self.row_end
+        SpMM_push(self.matrix, N, B, replicas.full[r0:r1], replicas.peer_panels(r0, N), stream)
+        _current_waits_for(stream, replicas.full)
+        flag = torch.zeros(1, device=replicas.full.device)
+        try:
+            dist.all_reduce(flag, group=group)
+        except (RuntimeError, dist.DistError) as e:
+            raise PeerLost(f"the barrier after the fused SpMM all-gather failed: {e}") from e
+        return replicas.full
+
     def sddmm(self, N: int, lhs_panel, rhs, outputs, stream=None):
         """Per-workset SDDMM outputs of this panel (lhs_panel holds the panel's rows)."""
         SDDMM(self.matrix, N, lhs_panel, rhs, outputs, stream)
@@ -137,3 +157,43 @@ class ShardedPowerSparse:
 
     def close(self):
         self.matrix.close()
+
+
+class Replicas:
+    """Every rank's full copy (``full``: [rows, N] float32 on this rank's GPU) of a
+    row-partitioned result, each opened on every other rank through CUDA IPC, so
+    that ps_spmm_push can store a rank's finished rows into all the copies.  Every
+    rank of ``group`` constructs it with the same shape (a collective); ``close``
+    releases the peers' mappings (every rank must close before any frees ``full``)."""
+
+    def __init__(self, rows: int, N: int, device, group=None):
+        import torch
+        import torch.distributed as dist
+        self.N = N
+        self.full = torch.zeros((rows, N), dtype=torch.float32, device=device)
+        rank, world = dist.get_rank(group), dist.get_world_size(group)
+        handle, offset = ipc_export(self.full)
+        shared = [None] * world
+        dist.all_gather_object(shared, (handle, offset), group=group)
+        self._bases, self._peers = [], []
+        try:
+            for r in range(world):
+                if r == rank:
+                    continue
+                base = ipc_open(shared[r][0])
+                self._bases.append(base)
+                self._peers.append(base + shared[r][1])
+        except Exception:
+            self.close()
+            raise
+
+    def peer_panels(self, row0: int, N: int) -> list:
+        """Addresses of row ``row0`` in every peer's copy."""
+        if N != self.N:
+            raise ValueError(f"the replicas hold rows of {self.N} floats, not {N}")
+        return [p + row0 * N * 4 for p in self._peers]
+
+    def close(self) -> None:
+        for b in self._bases:
+            ipc_close(b)
+        self._bases, self._peers = [], []
