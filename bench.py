@@ -412,6 +412,8 @@ def main() -> None:
         tg = timed(lambda: allgather_rows(C, cuts), 5)
         extra["allgather_c"] = {"ms": round(tg, 3), "bytes_per_gpu_in": int(full.numel() * 4 - C.numel() * 4)}
         del full
+        extra["spmm_allgather_fused"] = fused_allgather(psb, m, B, C, N, cuts, rank, device, stream, dist, timed,
+                                                        allgather_rows)
 
     if world == 1:
         e2e = e2e_whole(psb, m, panel, B, C, N, device, stream, args.e2e_steps, nnz_total, args.e2e_chunks)
@@ -609,6 +611,51 @@ def e2e_sharded(psb, m, panel, B, N, rank, world, device, stream, dist, steps, n
             "bytes_per": "rank", "h2d_bytes_per_step_all_ranks": int(h_slice.numel() * 4 * world),
             "allgather_bytes_in_per_rank": int((world - 1) * per * N * 4),
             "gathered_B_matches": same, "ms_per_step": round(ms, 3), "steps": steps, "copy_chunks": chunks}
+
+
+def fused_allgather(psb, m, B, C, N, cuts, rank, device, stream, dist, timed, allgather_rows) -> dict:
+    """SpMM with the all-gather of C fused in (ps_spmm_push over CUDA IPC: each rank's
+    finished rows go straight into every other rank's replica from the kernel; a
+    one-element all-reduce after it marks every replica complete), timed against
+    SpMM followed by the NCCL all-gather of the panels.  The replica after one fused
+    call is checked against the all-gathered result of a plain SpMM."""
+    import torch
+    from powersparse_b200.distributed import Replicas
+    rows_total = int(cuts[-1])
+    r0, r1 = int(cuts[rank]), int(cuts[rank + 1])
+    reps = Replicas(rows_total, N, device)
+    peers = reps.peer_panels(r0, N)
+    flag = torch.zeros(1, device=device)
+    panel_out = reps.full[r0:r1]
+
+    def fused():
+        psb.SpMM_push(m, N, B, panel_out, peers, stream)
+        dist.all_reduce(flag)
+
+    def separate():
+        psb.SpMM(m, N, B, C, stream)
+        allgather_rows(C, cuts)
+
+    ms_fused = timed(fused, 5)
+    ms_sep = timed(separate, 5)
+    reps.full.zero_()
+    C.zero_()
+    torch.cuda.synchronize(device)
+    dist.barrier()
+    fused()
+    psb.SpMM(m, N, B, C, stream)
+    ref = allgather_rows(C, cuts)
+    torch.cuda.synchronize(device)
+    ok = torch.tensor([1.0 if bool(torch.allclose(reps.full, ref, rtol=1e-4, atol=1e-5)) else 0.0], device=device)
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    torch.cuda.synchronize(device)
+    dist.barrier()  # no rank frees its replica while a peer still maps it
+    reps.close()
+    dist.barrier()
+    del ref
+    return {"ms": round(ms_fused, 3), "separate_ms": round(ms_sep, 3),
+            "replica_bytes_out_per_gpu": int((r1 - r0) * N * 4 * (dist.get_world_size() - 1)),
+            "replicas_match_allgather": bool(ok.item() == 1.0)}
 
 
 def _run_pipeline(step, events, stream, device, steps, dist) -> float:

@@ -72,3 +72,55 @@ def test_sharded_spmm_sddmm_on_two_gpus(tmp_path):
         exp = oracle.sddmm(L, X[cuts[r]:cuts[r + 1]], Y)
         for s in range(L.S):
             assert oracle.close(np.load(tmp_path / f"sddmm{r}_{s}.npy"), exp[s], ATOL, RTOL).all()
+
+
+def _push_worker(rank, world, port, result_dir):
+    import datetime
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    try:
+        import powersparse_b200 as psb
+        from powersparse_b200 import synth
+        from powersparse_b200.distributed import Replicas, ShardedPowerSparse, panel_csr
+        m = synth.chung_lu(20000, 30, 2000, 2.1, seed=37)
+        cuts = psb.partition_rows(m.row_ptr, world)
+        panel = panel_csr(m, int(cuts[rank]), int(cuts[rank + 1]))
+        shard = ShardedPowerSparse(m.row_ptr, panel, rank, world, sm_count=2)
+        for n in (32, 128):
+            B = torch.from_numpy(synth.dense(m.cols, n, 11 + n)).to(dev)
+            reps = Replicas(m.rows, n, dev)
+            reps.full.fill_(float("nan"))
+            reps.full[shard.row_begin:shard.row_end].zero_()
+            dist.barrier()
+            full = shard.spmm_replicated(n, B, reps)
+            torch.cuda.synchronize()
+            np.save(os.path.join(result_dir, f"push{n}_{rank}.npy"), full.cpu().numpy())
+            dist.barrier()  # no rank frees its replica while a peer still maps it
+            reps.close()
+            dist.barrier()
+        shard.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_fused_allgather_spmm_on_two_gpus(tmp_path):
+    """ps_spmm_push over CUDA IPC: each rank's replica holds every panel, equal across
+    ranks bit for bit and to the FP64 product within tolerance."""
+    from helpers import ATOL, RTOL
+    from oracle import oracle
+    from powersparse_b200 import synth
+    world = 2
+    mp.start_processes(_push_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, start_method="spawn")
+    m = synth.chung_lu(20000, 30, 2000, 2.1, seed=37)
+    for n in (32, 128):
+        expected = oracle.spmm(m.row_ptr, m.col_ind, m.values, synth.dense(m.cols, n, 11 + n))
+        got = [np.load(tmp_path / f"push{n}_{r}.npy") for r in range(world)]
+        for r in range(world):
+            assert not np.isnan(got[r]).any(), f"rank {r}: rows missing from the replica (N={n})"
+            assert oracle.close(got[r], expected, ATOL, RTOL).all(), f"rank {r} N={n}"
+        assert np.array_equal(got[0], got[1]), f"replicas differ between ranks (N={n})"

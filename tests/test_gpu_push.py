@@ -39,18 +39,21 @@ def _with_wide_and_empty_rows(seed: int) -> synth.Csr:
 
 
 def _matrices():
-    return {"config2_scaled": synth.config_matrix(2, scale=0.01), "wide_and_empty": _with_wide_and_empty_rows(3)}
+    # (matrix, SM count of the workset heuristic): one SM gives the small matrix
+    # block worksets with groups of up to 256 elements, so its long rows are wide.
+    return {"config2_scaled": (synth.config_matrix(2, scale=0.01), 0),
+            "wide_and_empty": (_with_wide_and_empty_rows(3), 1)}
 
 
 @pytest.mark.parametrize("name", ["config2_scaled", "wide_and_empty"])
 @pytest.mark.parametrize("n", [32, 64, 128])
 def test_every_row_reaches_every_replica(name, n):
-    A = _matrices()[name]
+    A, sm = _matrices()[name]
     B_host = dense_inputs(A.cols, n, 31 + n)
     expected = oracle.spmm(A.row_ptr, A.col_ind, A.values, B_host)
-    with psb.PowerSparseMatrixGPU(A.rows, A.cols, A.nnz, A.row_ptr, A.col_ind, A.values) as m:
+    with psb.PowerSparseMatrixGPU(A.rows, A.cols, A.nnz, A.row_ptr, A.col_ind, A.values, sm_count=sm) as m:
         if name == "wide_and_empty":
-            assert m.wide_rows > 0  # the fold path finishes these rows
+            assert m.wide_rows == 3  # the fold path finishes these rows
         B = torch.from_numpy(B_host).cuda()
         C = torch.zeros((A.rows, n), device="cuda")
         # Replicas hold this panel at an offset, as a full replica of several panels would.
@@ -63,13 +66,17 @@ def test_every_row_reaches_every_replica(name, n):
         for k, r in enumerate(replicas):
             assert torch.equal(r[5:5 + A.rows], C), f"replica {k} differs from C"
             assert torch.isnan(r[:5]).all() and torch.isnan(r[5 + A.rows:]).all(), "wrote outside the panel"
-        # A second call without zeroing C accumulates; the replicas get the new rows.
+        # A second call without zeroing C adds into it as SpMM does (rows with a single
+        # residue group are stored, the rest added); the replicas get the new rows.
         for r in replicas:
             r.fill_(float("nan"))
         psb.SpMM_push(m, n, B, C, peers)
+        C_twice = torch.zeros_like(C)
+        psb.SpMM(m, n, B, C_twice)
+        psb.SpMM(m, n, B, C_twice)
         torch.cuda.synchronize()
-        ok = oracle.close(C.cpu().numpy(), 2 * expected, ATOL, RTOL)
-        assert ok.all(), f"{(~ok).sum()} elements outside tolerance after the second call"
+        ok = oracle.close(C.cpu().numpy(), C_twice.cpu().numpy().astype(np.float64), ATOL, RTOL)
+        assert ok.all(), f"{(~ok).sum()} elements differ from two plain SpMM calls"
         for k, r in enumerate(replicas):
             assert torch.equal(r[5:5 + A.rows], C), f"replica {k} differs from C after the second call"
 
@@ -77,7 +84,8 @@ def test_every_row_reaches_every_replica(name, n):
 def test_push_matches_plain_spmm_and_handles_no_peers():
     A = _with_wide_and_empty_rows(4)
     B_host = dense_inputs(A.cols, 128, 9)
-    with psb.PowerSparseMatrixGPU(A.rows, A.cols, A.nnz, A.row_ptr, A.col_ind, A.values) as m:
+    with psb.PowerSparseMatrixGPU(A.rows, A.cols, A.nnz, A.row_ptr, A.col_ind, A.values, sm_count=1) as m:
+        assert m.wide_rows > 0
         B = torch.from_numpy(B_host).cuda()
         C_plain = torch.zeros((A.rows, 128), device="cuda")
         psb.SpMM(m, 128, B, C_plain)
