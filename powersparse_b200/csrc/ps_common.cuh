@@ -137,8 +137,11 @@ struct StreamArray {
   }
   StreamArray(const StreamArray&) = delete;
   StreamArray& operator=(const StreamArray&) = delete;
-  ~StreamArray() {
+  ~StreamArray() { release(); }
+  // Gives the buffer back now (in stream order).
+  void release() noexcept {
     if (ptr) cudaFreeAsync(ptr, stream);
+    ptr = nullptr;
   }
   T* get() const { return ptr; }
 };

@@ -723,8 +723,11 @@ Matrix* build_matrix(int rows, int cols, int nnz, const int* row_ptr, const int*
   cudaStream_t st = nullptr;  // preprocessing is synchronous, like the reference constructor
   const int kBlocks = 16 * device_sms();
 
-  DeviceArray<int> d_row_ptr(size_t(rows) + 1), d_col(nnz);
-  DeviceArray<float> d_val(nnz);
+  // Temporaries come from the scratch pool (stream-ordered, no cudaMalloc / cudaFree
+  // and the device-wide waits cudaFree implies); arrays the matrix keeps are cudaMalloc'd.
+  DeviceArray<int> d_row_ptr(size_t(rows) + 1);
+  StreamArray<int> d_col(nnz, st);
+  StreamArray<float> d_val(nnz, st);
   upload_pageable({{d_row_ptr.get(), row_ptr, sizeof(int) * (size_t(rows) + 1)},
                    {d_col.get(), col_ind, sizeof(int) * size_t(nnz)},
                    {d_val.get(), sp_data, sizeof(float) * size_t(nnz)}},
@@ -733,7 +736,7 @@ Matrix* build_matrix(int rows, int cols, int nnz, const int* row_ptr, const int*
 
   // --- Number of worksets (AnalyzeMatrix).
   {
-    DeviceArray<unsigned long long> counts(kSizeClasses);
+    StreamArray<unsigned long long> counts(kSizeClasses, st);
     PSB_CUDA(cudaMemsetAsync(counts.get(), 0, sizeof(unsigned long long) * kSizeClasses, st));
     workset_size_counts<<<grid_for(rows, 256, kBlocks), 256, 0, st>>>(d_row_ptr.get(), rows, counts.get());
     PSB_LAUNCH_CHECK();
@@ -753,7 +756,7 @@ Matrix* build_matrix(int rows, int cols, int nnz, const int* row_ptr, const int*
   trace.mark("worksets");
 
   // --- Column frequencies.
-  DeviceArray<int> d_col_nnz(cols);
+  StreamArray<int> d_col_nnz(cols, st);
   PSB_CUDA(cudaMemsetAsync(d_col_nnz.get(), 0, sizeof(int) * size_t(cols), st));
   col_histogram<<<grid_for(nnz, 256, kBlocks), 256, 0, st>>>(d_col.get(), nnz, d_col_nnz.get());
   PSB_LAUNCH_CHECK();
@@ -789,7 +792,7 @@ Matrix* build_matrix(int rows, int cols, int nnz, const int* row_ptr, const int*
   trace.mark("freq_sort");
 
   // --- Groups per workset and their source metadata.
-  DeviceArray<int> counts(size_t(S) * rows), prefix(size_t(S) * (size_t(rows) + 1));
+  StreamArray<int> counts(size_t(S) * rows, st), prefix(size_t(S) * (size_t(rows) + 1), st);
   row_group_counts<<<grid_for(rows, 256, kBlocks), 256, 0, st>>>(d_row_ptr.get(), rows, S, fine, counts.get());
   PSB_LAUNCH_CHECK();
   m->group_num.assign(S, 0);
@@ -800,15 +803,15 @@ Matrix* build_matrix(int rows, int cols, int nnz, const int* row_ptr, const int*
   }
   counts.release();
   const int G0 = m->group_num[0];
-  std::vector<DeviceArray<int>> src_des(S), src_start(S);
-  DeviceArray<int> res_size(G0);
-  DeviceArray<unsigned char> res_atomic_src(G0);
+  std::vector<std::unique_ptr<StreamArray<int>>> src_des(S), src_start(S);
+  StreamArray<int> res_size(G0, st);
+  StreamArray<unsigned char> res_atomic_src(G0, st);
   WorksetArrays wa{};
   for (int s = 0; s < S; ++s) {
-    src_des[s].reset(m->group_num[s]);
-    src_start[s].reset(m->group_num[s]);
-    wa.des[s] = src_des[s].get();
-    wa.start[s] = src_start[s].get();
+    src_des[s].reset(new StreamArray<int>(m->group_num[s], st));
+    src_start[s].reset(new StreamArray<int>(m->group_num[s], st));
+    wa.des[s] = src_des[s]->get();
+    wa.start[s] = src_start[s]->get();
     wa.groups[s] = m->group_num[s];
   }
   group_metadata<<<grid_for(rows, 256, kBlocks), 256, 0, st>>>(d_row_ptr.get(), rows, S, fine, prefix.get(), wa,
@@ -821,14 +824,14 @@ Matrix* build_matrix(int rows, int cols, int nnz, const int* row_ptr, const int*
   m->signature_len = signature_len;
   trace.mark("sig_bits_wait");
   const int words = m->signature_len / 32;
-  DeviceArray<int> d_sigbit(cols);
-  PSB_CUDA(cudaMemcpy(d_sigbit.get(), h_sigbit.data(), sizeof(int) * size_t(cols), cudaMemcpyHostToDevice));
-  std::vector<DeviceArray<uint32_t>> sig(S);
+  StreamArray<int> d_sigbit(cols, st);
+  PSB_CUDA(cudaMemcpyAsync(d_sigbit.get(), h_sigbit.data(), sizeof(int) * size_t(cols), cudaMemcpyHostToDevice, st));
+  std::vector<std::unique_ptr<StreamArray<uint32_t>>> sig(S);
   for (int s = 0; s < S; ++s) {
-    sig[s].reset(size_t(words) * m->group_num[s]);
+    sig[s].reset(new StreamArray<uint32_t>(size_t(words) * m->group_num[s], st));
     if (m->group_num[s])
-      PSB_CUDA(cudaMemsetAsync(sig[s].get(), 0, sizeof(uint32_t) * size_t(words) * m->group_num[s], st));
-    wa.sig[s] = sig[s].get();
+      PSB_CUDA(cudaMemsetAsync(sig[s]->get(), 0, sizeof(uint32_t) * size_t(words) * m->group_num[s], st));
+    wa.sig[s] = sig[s]->get();
   }
   group_signatures<<<grid_for(rows, 8, kBlocks), 256, 0, st>>>(d_row_ptr.get(), rows, S, fine, prefix.get(),
                                                                perm, d_col.get(), d_sigbit.get(), wa);
@@ -842,8 +845,8 @@ Matrix* build_matrix(int rows, int cols, int nnz, const int* row_ptr, const int*
   // The worksets are independent, so each sorts on its own stream; within one, all
   // word passes are queued without a host round trip (the buffer side of every
   // pass is kept on the device), and the order ends in order[s].
-  std::vector<DeviceArray<uint32_t>> order(S);
-  for (int s = 0; s < S; ++s) order[s].reset(m->group_num[s]);
+  std::vector<std::unique_ptr<StreamArray<uint32_t>>> order(S);
+  for (int s = 0; s < S; ++s) order[s].reset(new StreamArray<uint32_t>(m->group_num[s], st));
   {
     StreamSet streams(S, st);
     for (int s = 0; s < S; ++s) {
@@ -854,22 +857,22 @@ Matrix* build_matrix(int rows, int cols, int nnz, const int* row_ptr, const int*
       StreamArray<uint32_t> keys(2 * size_t(G), ss), idx_alt(G, ss);
       StreamArray<int> side(size_t(words) * per_word + 1, ss);
       PSB_CUDA(cudaMemsetAsync(side.get(), 0, sizeof(int), ss));
-      iota_u32(order[s].get(), G, ss);
+      uint32_t* ord = order[s]->get();
+      iota_u32(ord, G, ss);
       int pass = 0;
       for (int w = words - 1; w >= 0; --w) {
         signature_word_keys<<<grid_for(G, 256, kBlocks), 256, 0, ss>>>(
-            sig[s].get() + size_t(w) * G, order[s].get(), idx_alt.get(), side.get() + pass, G, keys.get(),
-            keys.get() + G);
+            sig[s]->get() + size_t(w) * G, ord, idx_alt.get(), side.get() + pass, G, keys.get(), keys.get() + G);
         PSB_LAUNCH_CHECK();
-        radix_sort_pairs_async<uint32_t>(keys.get(), order[s].get(), keys.get() + G, idx_alt.get(), size_t(G), 0,
-                                         32, side.get() + pass, ss);
+        radix_sort_pairs_async<uint32_t>(keys.get(), ord, keys.get() + G, idx_alt.get(), size_t(G), 0, 32,
+                                         side.get() + pass, ss);
         pass += per_word;
       }
-      take_from_alt(side.get() + pass, idx_alt.get(), order[s].get(), size_t(G), ss);
+      take_from_alt(side.get() + pass, idx_alt.get(), ord, size_t(G), ss);
     }
     streams.join();
   }
-  for (int s = 0; s < S; ++s) sig[s].release();
+  for (int s = 0; s < S; ++s) sig[s]->release();
   trace.mark("sig_sort");
 
   // --- Final worksets.
@@ -880,12 +883,12 @@ Matrix* build_matrix(int rows, int cols, int nnz, const int* row_ptr, const int*
   m->ws_size.assign(S, 0);
   DeviceArray<int> res_off(size_t(G0) + 1);
   {
-    DeviceArray<int> size_perm(G0);
+    StreamArray<int> size_perm(G0, st);
     DeviceArray<bool> atomic_out(G0);
     DeviceArray<int> des_out(G0);
     if (G0) {
-      permute_residue_meta<<<grid_for(G0, 256, kBlocks), 256, 0, st>>>(order[0].get(), G0, res_size.get(),
-                                                                        res_atomic_src.get(), src_des[0].get(),
+      permute_residue_meta<<<grid_for(G0, 256, kBlocks), 256, 0, st>>>(order[0]->get(), G0, res_size.get(),
+                                                                        res_atomic_src.get(), src_des[0]->get(),
                                                                         size_perm.get(), atomic_out.get(),
                                                                         des_out.get());
       PSB_LAUNCH_CHECK();
@@ -904,7 +907,7 @@ Matrix* build_matrix(int rows, int cols, int nnz, const int* row_ptr, const int*
     m->ws_size[s] = n;
     if (s > 0 && G) {
       DeviceArray<int> des_out(G);
-      permute_block_des<<<grid_for(G, 256, kBlocks), 256, 0, st>>>(order[s].get(), G, src_des[s].get(),
+      permute_block_des<<<grid_for(G, 256, kBlocks), 256, 0, st>>>(order[s]->get(), G, src_des[s]->get(),
                                                                    des_out.get());
       PSB_LAUNCH_CHECK();
       m->group_des[s] = des_out.release_ownership();
@@ -917,8 +920,8 @@ Matrix* build_matrix(int rows, int cols, int nnz, const int* row_ptr, const int*
     StreamArray<int> side(size_t(passes) + 1, st);
     PSB_CUDA(cudaMemsetAsync(side.get(), 0, sizeof(int), st));
     gather_group_elements<<<grid_for(G, 8, kBlocks), 256, 0, st>>>(
-        order[s].get(), G, s == 0 ? 0 : group_size(s), s == 0 ? res_off.get() : nullptr,
-        s == 0 ? res_size.get() : nullptr, src_start[s].get(), perm, d_col.get(), wcol, keys.get(),
+        order[s]->get(), G, s == 0 ? 0 : group_size(s), s == 0 ? res_off.get() : nullptr,
+        s == 0 ? res_size.get() : nullptr, src_start[s]->get(), perm, d_col.get(), wcol, keys.get(),
         vals.get());
     PSB_LAUNCH_CHECK();
     radix_sort_pairs_async<uint64_t>(keys.get(), vals.get(), keys_alt.get(), vals_alt.get(), size_t(n), 0,
