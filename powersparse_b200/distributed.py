@@ -177,9 +177,11 @@ class Replicas:
         dist.all_gather_object(shared, (handle, offset), group=group)
         self._bases, self._peers = [], []
         try:
-            for r in range(world):
-                if r == rank:
-                    continue
+            # Peers in ring order from this rank (rank+1, rank+2, ...): the push kernel
+            # stores to peers in list order, so at each position every rank sends to a
+            # different GPU instead of all of them to the same one.
+            for step in range(1, world):
+                r = (rank + step) % world
                 base = ipc_open(shared[r][0])
                 self._bases.append(base)
                 self._peers.append(base + shared[r][1])
