@@ -70,3 +70,48 @@ def test_panel_csr_slices_rows():
     lo, hi = m.row_ptr[100], m.row_ptr[260]
     assert np.array_equal(p.col_ind, m.col_ind[lo:hi])
     assert np.array_equal(np.diff(p.row_ptr), np.diff(m.row_ptr)[100:260])
+
+
+def _replicas_worker(rank, world, port, result_dir):
+    """Replicas on gloo with the CUDA IPC calls replaced by fakes: each rank "exports"
+    a handle naming its rank and a made-up base address; opening returns that base."""
+    import datetime
+    import json
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        import powersparse_b200.distributed as D
+        base_of = lambda r: (r + 1) << 40  # noqa: E731
+        opened, closed = [], []
+        D.ipc_export = lambda t: (bytes([rank]) * 64, 256 * (rank + 1))
+        D.ipc_open = lambda h: (opened.append(h[0]), base_of(h[0]))[1]
+        D.ipc_close = lambda b: closed.append(b)
+        reps = D.Replicas(100, 32, "cpu")
+        panels = reps.peer_panels(10, 32)
+        with pytest.raises(ValueError):
+            reps.peer_panels(10, 64)
+        reps.close()
+        with open(os.path.join(result_dir, f"replicas{rank}.json"), "w") as f:
+            json.dump({"opened": opened, "panels": panels, "closed": closed,
+                       "shape": list(reps.full.shape)}, f)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_replicas_open_peers_in_ring_order_on_gloo(tmp_path):
+    """Each rank opens every other rank's replica once, in ring order from itself; the
+    panel addresses are the peer's base + its export offset + row0 * N * 4 bytes; close
+    releases every mapping."""
+    import json
+    world = 4
+    mp.start_processes(_replicas_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world,
+                       start_method="spawn")
+    for rank in range(world):
+        with open(tmp_path / f"replicas{rank}.json") as f:
+            got = json.load(f)
+        ring = [(rank + s) % world for s in range(1, world)]
+        assert got["opened"] == ring
+        assert got["panels"] == [((r + 1) << 40) + 256 * (r + 1) + 10 * 32 * 4 for r in ring]
+        assert got["closed"] == [(r + 1) << 40 for r in ring]
+        assert got["shape"] == [100, 32]
