@@ -228,9 +228,10 @@ def main() -> None:
     ap.add_argument("--workload", choices=["cfg2", "cfg5"], default="cfg2",
                     help="cfg2: config 2 per GPU (weak scaling, default); cfg5: the config-5 R-MAT graph "
                          "(16.8M nodes, ~1B nnz) split over the GPUs (strong scaling)")
-    ap.add_argument("--profile-op", choices=["spmm", "sddmm"], default=None,
+    ap.add_argument("--profile-op", choices=["spmm", "sddmm", "spmm_push"], default=None,
                     help="only build the workload and run this operator at --n, --warmup + --steps times "
-                         "(a small, single-kernel process for profilers); prints one short JSON line")
+                         "(a small, single-kernel process for profilers; spmm_push pushes every finished "
+                         "row to one replica on this GPU); prints one short JSON line")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -472,6 +473,10 @@ def profile_op(psb, m, panel, args, device) -> None:
     if args.profile_op == "spmm":
         C = torch.zeros((panel.rows, N), dtype=torch.float32, device=device)
         run = lambda: psb.SpMM(m, N, B, C)
+    elif args.profile_op == "spmm_push":
+        C = torch.zeros((panel.rows, N), dtype=torch.float32, device=device)
+        replica = torch.zeros_like(C)
+        run = lambda: psb.SpMM_push(m, N, B, C, [replica.data_ptr()])
     else:
         X = dense_B(panel.rows, N, device, seed=202)
         outs = [torch.zeros(max(m.workset_size(s), 1), dtype=torch.float32, device=device)

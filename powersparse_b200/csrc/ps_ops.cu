@@ -281,7 +281,17 @@ __global__ void __launch_bounds__(kThreads, 4) spmm_fused(const SpmmArgs a) {
               const int row = w & 0x7fffffff;
               if (in_range(row, a.rows, kBadRow)) {
                 emit4(Cl + (long long)row * a.ldb, acc, w < 0);
-                if constexpr (kPush) push_if_finished<LG>(a, row, colofs, gm, l);
+                if constexpr (kPush) {
+                  // A stored group (w >= 0) is its row's only add of the launch (a residue
+                  // group never spans two tasks), so `acc` is the finished segment: it goes
+                  // to the peers at once, with no fence or countdown.
+                  if (w < 0) {
+                    push_if_finished<LG>(a, row, colofs, gm, l);
+                  } else {
+                    for (int k = 0; k < a.peers; ++k)
+                      __stcg(reinterpret_cast<float4*>(a.peer[k] + (long long)row * a.ldb + colofs), acc);
+                  }
+                }
               }
               acc = make_float4(0.f, 0.f, 0.f, 0.f);
             }
